@@ -1,0 +1,348 @@
+// cu_roaring B200 engine — bulk point queries, decompress, enumerate_ids,
+// promotion.
+//
+// decompress: one CTA per 65536-bit chunk of the OUTPUT (not per container,
+// as reference src/decompress.cu:8-87 does after a full memset), so every
+// output word is written exactly once with 16-byte stores, absent chunks
+// and the complement/tail mask included; no global atomics.
+// enumerate_ids: count -> tile scan -> one CTA per unit writes sorted IDs;
+// negated bitmaps enumerate the complement (the reference ignores
+// `negated`, src/to_csr.cu:36-131).
+#include <algorithm>
+
+#include "chunk_ops.cuh"
+#include "cu_roaring/device/make_view.cuh"
+#include "cu_roaring/device/roaring_warp_query.cuh"
+
+namespace crb {
+namespace {
+
+static_assert(sizeof(cr_gpu_roaring) == sizeof(cu_roaring::GpuRoaring), "ABI layout");
+static_assert(offsetof(cr_gpu_roaring, negated) == offsetof(cu_roaring::GpuRoaring, negated), "ABI");
+static_assert(offsetof(cr_gpu_roaring, _alloc_base) == offsetof(cu_roaring::GpuRoaring, _alloc_base), "ABI");
+static_assert(offsetof(cr_gpu_roaring, key_index) == offsetof(cu_roaring::GpuRoaring, key_index), "ABI");
+
+constexpr int kUnroll = 4;
+
+// Bulk contains: each warp answers 32*kUnroll consecutive candidates per
+// step (coalesced 128-byte ID loads, kUnroll independent lookups in flight)
+// and writes one 32-bit result word per 32 candidates via __ballot_sync.
+template <int MODE>
+__global__ void __launch_bounds__(256) k_contains(cu_roaring::GpuRoaringView v,
+                                                  const uint32_t* __restrict__ ids, uint64_t n,
+                                                  uint32_t* __restrict__ out)
+{
+  const uint32_t lane = threadIdx.x & 31;
+  const uint64_t n_words = (n + 31) / 32;
+  const uint64_t warp = (uint64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const uint64_t n_warps = (uint64_t(gridDim.x) * blockDim.x) >> 5;
+  for (uint64_t w0 = warp * kUnroll; w0 < n_words; w0 += n_warps * kUnroll) {
+    uint32_t id[kUnroll];
+    bool in[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const uint64_t i = (w0 + u) * 32 + lane;
+      in[u] = i < n;
+      id[u] = in[u] ? __ldcs(ids + i) : 0u;
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      bool hit = false;
+      if (in[u]) hit = MODE ? cu_roaring::warp_contains(v, id[u]) : v.contains(id[u]);
+      const uint32_t bits = __ballot_sync(0xFFFFFFFFu, hit);
+      if (lane == 0 && w0 + u < n_words) __stcs(out + w0 + u, bits);
+    }
+  }
+}
+
+// One CTA (256 threads) per output chunk.
+__global__ void __launch_bounds__(256) k_decompress(DevBitmap b, uint32_t* out, uint64_t out_words)
+{
+  __shared__ __align__(16) uint64_t sm[1024];
+  const uint32_t key = blockIdx.x;
+  const ContainerRef c = dev_container(b, dev_lookup(b, key));
+  uint64_t w[4];
+  container_words<256, 4>(b, c, sm, w);
+  const uint32_t valid = chunk_valid_bits(key, b.universe);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint64_t m = word_mask(4 * threadIdx.x + i, valid);
+    w[i] = (b.negated ? ~w[i] : w[i]) & m;
+  }
+  const uint64_t g = uint64_t(key) * kChunkWords32 + 8ull * threadIdx.x;
+  if (g + 8 <= out_words && (reinterpret_cast<uintptr_t>(out) & 15u) == 0) {
+    uint4* p = reinterpret_cast<uint4*>(out + g);
+    p[0] = make_uint4(uint32_t(w[0]), uint32_t(w[0] >> 32), uint32_t(w[1]), uint32_t(w[1] >> 32));
+    p[1] = make_uint4(uint32_t(w[2]), uint32_t(w[2] >> 32), uint32_t(w[3]), uint32_t(w[3] >> 32));
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (g + i < out_words) out[g + i] = uint32_t(w[i >> 1] >> (32 * (i & 1)));
+  }
+}
+
+// Units: containers (plain) or every chunk of the universe (negated).
+__device__ __forceinline__ uint32_t unit_key(const DevBitmap& b, uint32_t u)
+{
+  return b.negated ? u : __ldg(b.keys + u);
+}
+
+__global__ void k_enum_count(DevBitmap b, uint32_t n_units, uint32_t* counts)
+{
+  const uint32_t u = blockIdx.x * blockDim.x + threadIdx.x;
+  if (u >= n_units) return;
+  const uint32_t key = unit_key(b, u);
+  const int idx = b.negated ? dev_lookup(b, key) : static_cast<int>(u);
+  const uint32_t stored = container_count(b, dev_container(b, idx));
+  counts[u] = b.negated ? chunk_valid_bits(key, b.universe) - stored : stored;
+}
+
+constexpr int kScanTile = 1024;
+
+__global__ void __launch_bounds__(kScanTile) k_scan_tiles(const uint32_t* v, uint32_t n,
+                                                          unsigned long long* tile_sums)
+{
+  __shared__ unsigned long long s_red[32];
+  const uint32_t i = blockIdx.x * kScanTile + threadIdx.x;
+  const unsigned long long x = i < n ? v[i] : 0u;
+  const unsigned long long t = block_sum<kScanTile, unsigned long long>(x, s_red);
+  if (threadIdx.x == 0) tile_sums[blockIdx.x] = t;
+}
+
+__global__ void __launch_bounds__(kScanTile) k_scan_apply(const uint32_t* v, uint32_t n,
+                                                          const unsigned long long* tile_sums,
+                                                          unsigned long long* prefix)
+{
+  __shared__ unsigned long long s_red[32];
+  __shared__ unsigned long long s_base;
+  if (threadIdx.x == 0) {
+    unsigned long long b = 0;
+    for (uint32_t j = 0; j < blockIdx.x; ++j) b += tile_sums[j];
+    s_base = b;
+  }
+  __syncthreads();
+  const uint32_t i = blockIdx.x * kScanTile + threadIdx.x;
+  const unsigned long long x = i < n ? v[i] : 0u;
+  unsigned long long tot;
+  const unsigned long long p = block_exclusive_scan<kScanTile, unsigned long long>(x, s_red, &tot);
+  if (i < n) prefix[i] = s_base + p;
+}
+
+template <class T>
+__global__ void __launch_bounds__(256) k_enum_emit(DevBitmap b, const unsigned long long* prefix,
+                                                   T* out)
+{
+  __shared__ __align__(16) uint64_t sm[1024];
+  __shared__ uint32_t s_red[8];
+  const uint32_t u = blockIdx.x;
+  const uint32_t key = unit_key(b, u);
+  const int idx = b.negated ? dev_lookup(b, key) : static_cast<int>(u);
+  const ContainerRef c = dev_container(b, idx);
+  T* dst = out + prefix[u];
+  const uint32_t hi = key << 16;
+  if (!b.negated && c.type == kArray) {
+    const uint16_t* a = b.array + (c.off >> 1);
+    for (uint32_t j = threadIdx.x; j < c.card; j += 256) dst[j] = static_cast<T>(hi | __ldg(a + j));
+    return;
+  }
+  uint64_t w[4];
+  container_words<256, 4>(b, c, sm, w);
+  if (b.negated) {
+    const uint32_t valid = chunk_valid_bits(key, b.universe);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) w[i] = ~w[i] & word_mask(4 * threadIdx.x + i, valid);
+  }
+  uint32_t cnt = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) cnt += __popcll(w[i]);
+  uint32_t total;
+  uint32_t pos = block_exclusive_scan<256>(cnt, s_red, &total);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint64_t x = w[i];
+    while (x) {
+      dst[pos++] = static_cast<T>(hi | ((4 * threadIdx.x + i) * 64 + __ffsll(x) - 1));
+      x &= x - 1;
+    }
+  }
+}
+
+// Promotion: container i becomes BITMAP slot i.
+__global__ void __launch_bounds__(256) k_promote(DevBitmap b, cr_gpu_roaring out)
+{
+  __shared__ __align__(16) uint64_t sm[1024];
+  __shared__ uint32_t s_red[8];
+  const uint32_t i = blockIdx.x;
+  const ContainerRef c = dev_container(b, static_cast<int>(i));
+  uint64_t w[4];
+  container_words<256, 4>(b, c, sm, w);
+  uint4* dst = reinterpret_cast<uint4*>(out.bitmap_data + size_t(i) * 1024) + 2 * threadIdx.x;
+  dst[0] = make_uint4(uint32_t(w[0]), uint32_t(w[0] >> 32), uint32_t(w[1]), uint32_t(w[1] >> 32));
+  dst[1] = make_uint4(uint32_t(w[2]), uint32_t(w[2] >> 32), uint32_t(w[3]), uint32_t(w[3] >> 32));
+  uint32_t cnt = 0;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) cnt += __popcll(w[k]);
+  const uint32_t total = block_sum<256>(cnt, s_red);
+  if (threadIdx.x == 0) {
+    const uint16_t key = __ldg(b.keys + i);
+    out.keys[i] = key;
+    out.types[i] = kBitmap;
+    out.offsets[i] = i * kBitmapBytes;
+    out.cardinalities[i] = static_cast<uint16_t>(total & 0xFFFFu);
+    if (key <= out.max_key) out.key_index[key] = static_cast<uint16_t>(i);
+  }
+}
+
+cu_roaring::GpuRoaringView view_of(const cr_gpu_roaring* bm)
+{
+  return cu_roaring::make_view(*reinterpret_cast<const cu_roaring::GpuRoaring*>(bm));
+}
+
+template <class T>
+void enumerate(const cr_gpu_roaring* bm, T* out, cudaStream_t s)
+{
+  if (bm->total_cardinality == 0) return;
+  CR_REQUIRE(out != nullptr, "enumerate_ids: null output");
+  Scratch holder;
+  const DevBitmap b = make_dev(bm, holder, s);
+  const uint32_t n_units = bm->negated ? n_chunks_for(bm->universe_size) : bm->n_containers;
+  if (n_units == 0) return;
+  const uint32_t n_tiles = div_up(n_units, kScanTile);
+  Scratch scr(size_t(n_units) * 4 + size_t(n_units) * 8 + size_t(n_tiles) * 8 + 16, s);
+  unsigned long long* prefix = scr.as<unsigned long long>();
+  unsigned long long* tiles = prefix + n_units;
+  uint32_t* counts = reinterpret_cast<uint32_t*>(tiles + n_tiles);
+  k_enum_count<<<div_up(n_units, 256), 256, 0, s>>>(b, n_units, counts);
+  k_scan_tiles<<<n_tiles, kScanTile, 0, s>>>(counts, n_units, tiles);
+  k_scan_apply<<<n_tiles, kScanTile, 0, s>>>(counts, n_units, tiles, prefix);
+  k_enum_emit<T><<<n_units, 256, 0, s>>>(b, prefix, out);
+  CR_CUDA(cudaGetLastError());
+}
+
+void promote_to_bitmap(const cr_gpu_roaring* in, cr_gpu_roaring* out, cudaStream_t s)
+{
+  cr_gpu_roaring r{};
+  r.universe_size = in->universe_size;
+  r.total_cardinality = in->total_cardinality;
+  r.negated = in->negated;
+  r.n_containers = in->n_containers;
+  r.n_bitmap_containers = in->n_containers;
+  if (in->n_containers == 0) { *out = r; return; }
+  uint32_t max_key = max_key_for(in->universe_size);
+  if (in->key_index == nullptr) max_key = 65535;  // keys not checked on the host
+  r.max_key = max_key;
+  alloc_result(&r, s);
+  Scratch holder;
+  const DevBitmap b = make_dev(in, holder, s);
+  CR_CUDA(cudaMemsetAsync(r.key_index, 0xFF, (size_t(max_key) + 1) * 2, s));
+  k_promote<<<in->n_containers, 256, 0, s>>>(b, r);
+  CR_CUDA(cudaGetLastError());
+  *out = r;
+}
+
+}  // namespace
+}  // namespace crb
+
+using namespace crb;
+
+extern "C" int cr_contains_batch(const cr_gpu_roaring* bm, const uint32_t* d_ids, uint64_t n,
+                                 uint32_t* d_out_bits, int mode, cr_stream_t stream)
+{
+  CR_API_BEGIN
+  CR_REQUIRE(bm != nullptr, "cr_contains_batch: null bitmap");
+  CR_REQUIRE(mode == 0 || mode == 1, "cr_contains_batch: mode must be 0 or 1");
+  if (n == 0) return CR_OK;
+  CR_REQUIRE(d_ids && d_out_bits, "cr_contains_batch: null buffer");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const cu_roaring::GpuRoaringView v = view_of(bm);
+  const uint64_t words = (n + 31) / 32;
+  const uint64_t want = (words + 8 * kUnroll - 1) / (8 * kUnroll);
+  const int grid = static_cast<int>(std::max<uint64_t>(1, std::min<uint64_t>(want, uint64_t(sm_count()) * 8)));
+  if (mode) k_contains<1><<<grid, 256, 0, s>>>(v, d_ids, n, d_out_bits);
+  else k_contains<0><<<grid, 256, 0, s>>>(v, d_ids, n, d_out_bits);
+  CR_CUDA(cudaGetLastError());
+  CR_API_END
+}
+
+extern "C" int cr_decompress_to_bitset(const cr_gpu_roaring* bm, uint32_t* d_output,
+                                       uint32_t output_words, cr_stream_t stream)
+{
+  CR_API_BEGIN
+  CR_REQUIRE(bm != nullptr, "cr_decompress_to_bitset: null bitmap");
+  if (output_words == 0) return CR_OK;
+  CR_REQUIRE(d_output != nullptr, "cr_decompress_to_bitset: null output");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  Scratch holder;
+  const DevBitmap b = make_dev(bm, holder, s);
+  k_decompress<<<div_up(output_words, kChunkWords32), 256, 0, s>>>(b, d_output, output_words);
+  CR_CUDA(cudaGetLastError());
+  CR_API_END
+}
+
+extern "C" int cr_decompress_to_bitset_alloc(const cr_gpu_roaring* bm, cr_stream_t stream,
+                                             uint32_t** d_out)
+{
+  CR_API_BEGIN
+  CR_REQUIRE(bm && d_out, "cr_decompress_to_bitset_alloc: null argument");
+  *d_out = nullptr;
+  const uint32_t words = div_up(bm->universe_size, 32);
+  if (words == 0) return CR_OK;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  uint32_t* p = static_cast<uint32_t*>(dev_alloc(size_t(words) * 4, s));
+  const int rc = cr_decompress_to_bitset(bm, p, words, stream);
+  if (rc != CR_OK) { cudaFreeAsync(p, s); return rc; }
+  *d_out = p;
+  CR_API_END
+}
+
+extern "C" int cr_enumerate_ids_i64(const cr_gpu_roaring* bm, int64_t* d_output, cr_stream_t stream)
+{
+  CR_API_BEGIN
+  CR_REQUIRE(bm != nullptr, "cr_enumerate_ids: null bitmap");
+  enumerate<long long>(bm, reinterpret_cast<long long*>(d_output), reinterpret_cast<cudaStream_t>(stream));
+  CR_API_END
+}
+
+extern "C" int cr_enumerate_ids_u32(const cr_gpu_roaring* bm, uint32_t* d_output, cr_stream_t stream)
+{
+  CR_API_BEGIN
+  CR_REQUIRE(bm != nullptr, "cr_enumerate_ids: null bitmap");
+  enumerate<uint32_t>(bm, d_output, reinterpret_cast<cudaStream_t>(stream));
+  CR_API_END
+}
+
+extern "C" int cr_enumerate_ids_alloc(const cr_gpu_roaring* bm, cr_stream_t stream, int64_t** d_out)
+{
+  CR_API_BEGIN
+  CR_REQUIRE(bm && d_out, "cr_enumerate_ids_alloc: null argument");
+  *d_out = nullptr;
+  if (bm->total_cardinality == 0) return CR_OK;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int64_t* p = static_cast<int64_t*>(dev_alloc(bm->total_cardinality * 8, s));
+  const int rc = cr_enumerate_ids_i64(bm, p, stream);
+  if (rc != CR_OK) { cudaFreeAsync(p, s); return rc; }
+  *d_out = p;
+  CR_API_END
+}
+
+extern "C" int cr_promote_to_bitmap(const cr_gpu_roaring* bm, cr_stream_t stream, cr_gpu_roaring* out)
+{
+  CR_API_BEGIN
+  CR_REQUIRE(bm && out, "cr_promote_to_bitmap: null argument");
+  promote_to_bitmap(bm, out, reinterpret_cast<cudaStream_t>(stream));
+  CR_API_END
+}
+
+// Reference src/promote.cu:369-385: promote iff AUTO resolves to ALL and the
+// input has non-bitmap containers, else an independent deep copy.
+extern "C" int cr_promote_auto(const cr_gpu_roaring* bm, cr_stream_t stream, int device_id,
+                               cr_gpu_roaring* out)
+{
+  CR_API_BEGIN
+  CR_REQUIRE(bm && out, "cr_promote_auto: null argument");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const uint32_t t = resolve_auto(bm->universe_size, device_id);
+  if (t == 0 && (bm->n_array_containers || bm->n_run_containers)) promote_to_bitmap(bm, out, s);
+  else deep_copy(bm, out, s);
+  CR_API_END
+}

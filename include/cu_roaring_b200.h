@@ -1,0 +1,200 @@
+/*
+ * cu_roaring B200 engine — C ABI of libcuroaring_b200.so.
+ *
+ * Every host entry point of the reference C++ API has one `cr_*` function
+ * here (plain pointers and sizes, no C++ types), so that a C++ shim
+ * (include/cu_roaring/detail/\*.cuh), a ctypes/cffi binding or any other FFI
+ * can bind it. Each function returns CR_OK (0) or a negative cr_status; the
+ * message of the last failure on the calling thread is cr_last_error_string().
+ *
+ * Ownership: functions with a `cr_gpu_roaring* out` parameter allocate ONE
+ * stream-ordered device block (cudaMallocAsync on `stream`) and store its
+ * base in out->_alloc_base; release it with cr_gpu_roaring_free[_async].
+ * Functions that build a new bitmap synchronise `stream` (its host-side
+ * fields — counts and sizes — must be known on return); all others are purely
+ * stream-ordered.
+ *
+ * Streams are passed as cr_stream_t, which is ABI-identical to cudaStream_t
+ * (NULL = the legacy default stream).
+ */
+#ifndef CU_ROARING_B200_H
+#define CU_ROARING_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* cr_stream_t;
+
+/* Byte-for-byte the layout of cu_roaring::GpuRoaring
+ * (reference include/cu_roaring/types.cuh:15-54). `types` points at u8 tags
+ * (0 ARRAY, 1 BITMAP, 2 RUN); `negated` is a C++ bool (one byte). */
+typedef struct cr_gpu_roaring {
+  uint16_t* keys;
+  uint8_t*  types;
+  uint32_t* offsets;
+  uint16_t* cardinalities;
+  uint32_t  n_containers;
+  uint32_t  universe_size;
+  uint64_t  total_cardinality;
+  uint64_t* bitmap_data;
+  uint32_t  n_bitmap_containers;
+  uint16_t* array_data;
+  uint32_t  n_array_containers;
+  uint32_t  array_pool_bytes;
+  uint16_t* run_data;
+  uint32_t  n_run_containers;
+  uint32_t  run_pool_bytes;
+  uint16_t* key_index;
+  uint32_t  max_key;
+  uint8_t   negated;
+  void*     _alloc_base;
+} cr_gpu_roaring;
+
+typedef enum cr_status {
+  CR_OK              = 0,
+  CR_ERR_INVALID     = -1, /* bad argument (null pointer, size, op code)      */
+  CR_ERR_CUDA        = -2, /* a CUDA runtime call failed                       */
+  CR_ERR_OOM         = -3, /* device allocation failed                          */
+  CR_ERR_RANGE       = -4, /* an input ID is >= universe_size                   */
+  CR_ERR_DEVICE      = -5, /* a kernel raised its device-side error flag        */
+  CR_ERR_UNSUPPORTED = -6  /* configuration not supported by this build         */
+} cr_status;
+
+/* Promotion thresholds (reference include/cu_roaring/detail/promote.cuh:38-40). */
+#define CR_PROMOTE_KEEP_DEFAULT 4096u
+#define CR_PROMOTE_ALL          0u
+#define CR_PROMOTE_AUTO         0xFFFFFFFFu
+
+/* Set operations (reference include/cu_roaring/detail/set_ops.cuh:7-12). */
+#define CR_OP_AND    0
+#define CR_OP_OR     1
+#define CR_OP_ANDNOT 2
+#define CR_OP_XOR    3
+
+const char* cr_last_error_string(void);
+/* Library version string ("cu_roaring_b200 <semver> sm_100a"). */
+const char* cr_version(void);
+
+/* ---- Construction --------------------------------------------------------- */
+
+/* Replaces upload_from_ids (reference src/upload_ids.cu:567-591,
+ * include/cu_roaring/detail/upload_ids.cuh:19-24). Unsorted IDs with
+ * duplicates, in HOST memory. Stores the complement when the unique count is
+ * > universe_size/2. IDs >= universe_size are rejected with CR_ERR_RANGE. */
+int cr_upload_from_ids(const uint32_t* host_ids, uint32_t n_ids, uint32_t universe_size,
+                       cr_stream_t stream, uint32_t bitmap_threshold, cr_gpu_roaring* out);
+
+/* Same, IDs already in DEVICE memory (no reference counterpart; the reference
+ * always copies from the host, src/upload_ids.cu:302-313). */
+int cr_upload_from_device_ids(const uint32_t* d_ids, uint64_t n_ids, uint32_t universe_size,
+                              cr_stream_t stream, uint32_t bitmap_threshold,
+                              cr_gpu_roaring* out);
+
+/* Replace upload_from_bitset / upload_from_device_bitset (reference
+ * src/upload_ids.cu:806-893, include/cu_roaring/detail/upload_ids.cuh:48-56).
+ * Bit i is (words[i/32] >> (i%32)) & 1. Bits >= universe_size are ignored.
+ * bitmap_threshold is an addition (the reference always builds all-BITMAP). */
+int cr_upload_from_bitset(const uint32_t* host_bitset, uint32_t n_words,
+                          uint32_t universe_size, cr_stream_t stream,
+                          uint32_t bitmap_threshold, cr_gpu_roaring* out);
+int cr_upload_from_device_bitset(const uint32_t* d_bitset, uint32_t n_words,
+                                 uint32_t universe_size, cr_stream_t stream,
+                                 uint32_t bitmap_threshold, cr_gpu_roaring* out);
+
+/* Replaces gpu_roaring_free / gpu_roaring_free_async (reference
+ * src/upload.cpp:318-350). Resets *bm to the empty state. */
+int cr_gpu_roaring_free(cr_gpu_roaring* bm);
+int cr_gpu_roaring_free_async(cr_gpu_roaring* bm, cr_stream_t stream);
+
+/* ---- Promotion ------------------------------------------------------------- */
+
+/* Replaces resolve_auto_threshold (reference src/promote.cu:334-367):
+ * PROMOTE_ALL iff 2*ceil(U/8) > L2 bytes of the device (-1 = current). */
+int cr_resolve_auto_threshold(uint32_t universe_size, int device_id, uint32_t* out_threshold);
+/* Replace promote_to_bitmap, promote_auto, gpu_roaring_deep_copy
+ * (reference src/promote.cu:173-385). Stream-ordered, no host sync. */
+int cr_promote_to_bitmap(const cr_gpu_roaring* bm, cr_stream_t stream, cr_gpu_roaring* out);
+int cr_promote_auto(const cr_gpu_roaring* bm, cr_stream_t stream, int device_id,
+                    cr_gpu_roaring* out);
+int cr_deep_copy(const cr_gpu_roaring* bm, cr_stream_t stream, cr_gpu_roaring* out);
+
+/* ---- Set algebra ----------------------------------------------------------- */
+
+/* Replaces set_operation (reference src/set_ops.cu:567-1207). */
+int cr_set_operation(const cr_gpu_roaring* a, const cr_gpu_roaring* b, int op,
+                     cr_stream_t stream, cr_gpu_roaring* out);
+/* Replace multi_and / multi_or (reference src/set_ops.cu:1715-1762).
+ * count <= 64. */
+int cr_multi_and(const cr_gpu_roaring* bitmaps, uint32_t count, cr_stream_t stream,
+                 cr_gpu_roaring* out);
+int cr_multi_or(const cr_gpu_roaring* bitmaps, uint32_t count, cr_stream_t stream,
+                cr_gpu_roaring* out);
+
+/* ---- Export ------------------------------------------------------------------ */
+
+/* Replaces decompress_to_bitset (reference src/decompress.cu:104-162).
+ * Writes all output_words words (bits >= universe_size are zero). */
+int cr_decompress_to_bitset(const cr_gpu_roaring* bm, uint32_t* d_output,
+                            uint32_t output_words, cr_stream_t stream);
+/* Allocating form: ceil(U/32) words via cudaMallocAsync; free with cudaFree
+ * (or cudaFreeAsync). *out is NULL when universe_size == 0. */
+int cr_decompress_to_bitset_alloc(const cr_gpu_roaring* bm, cr_stream_t stream,
+                                  uint32_t** d_out);
+
+/* Replace enumerate_ids (reference src/to_csr.cu:161-220): the sorted IDs of
+ * the LOGICAL set (negation honoured), exactly total_cardinality values.
+ * The u32 form is an addition. */
+int cr_enumerate_ids_i64(const cr_gpu_roaring* bm, int64_t* d_output, cr_stream_t stream);
+int cr_enumerate_ids_u32(const cr_gpu_roaring* bm, uint32_t* d_output, cr_stream_t stream);
+int cr_enumerate_ids_alloc(const cr_gpu_roaring* bm, cr_stream_t stream, int64_t** d_out);
+
+/* ---- Bulk point queries ------------------------------------------------------ */
+
+/* Bulk form of GpuRoaringView::contains / warp_contains (reference
+ * include/cu_roaring/device/roaring_view.cuh:39, roaring_warp_query.cuh:16),
+ * as the reference benches use them (bench/bench_point_query.cu:123-146):
+ * bit i of d_out_bits (u32 words, ceil(n/32)) = contains(d_ids[i]).
+ * mode 0 = per-thread contains, 1 = warp_contains. */
+int cr_contains_batch(const cr_gpu_roaring* bm, const uint32_t* d_ids, uint64_t n,
+                      uint32_t* d_out_bits, int mode, cr_stream_t stream);
+
+/* ---- Fused filtered brute-force top-k (no reference counterpart; the
+ * reference only describes it, README.md:265-285) ---------------------------- */
+
+#define CR_METRIC_IP 0  /* larger inner product is better          */
+#define CR_METRIC_L2 1  /* smaller squared euclidean distance is better */
+
+/* Exact top-k over the database rows that the filter contains.
+ *   d_db      fp16 [n_rows x dim], row-major (dim == 128)
+ *   d_db_norms fp32 [n_rows] squared norms (L2 only; may be NULL for IP)
+ *   d_queries fp16 [n_queries x dim]
+ *   filter    rows r with contains(r) take part; NULL = all rows
+ *   row_offset global ID of row 0 (for sharded databases); the filter is
+ *             queried with row_offset + r and output IDs include it
+ *   k         1..256
+ *   d_out_dist fp32 [n_queries x k], best first (IP: scores, L2: distances)
+ *   d_out_ids  int64 [n_queries x k], -1 where fewer than k rows pass
+ * Scratch is allocated stream-ordered on `stream`. */
+int cr_filtered_topk(const uint16_t* d_db, const float* d_db_norms, uint64_t n_rows,
+                     uint32_t dim, const uint16_t* d_queries, uint32_t n_queries,
+                     const cr_gpu_roaring* filter, uint64_t row_offset, uint32_t k,
+                     int metric, float* d_out_dist, int64_t* d_out_ids, cr_stream_t stream);
+
+/* Squared L2 norms of fp16 rows (fp32 accumulate) for the L2 metric. */
+int cr_row_norms(const uint16_t* d_db, uint64_t n_rows, uint32_t dim, float* d_out,
+                 cr_stream_t stream);
+
+/* Merge `n_parts` per-shard top-k lists ([n_parts x n_queries x k], device)
+ * into one [n_queries x k] list (same ordering rules as cr_filtered_topk). */
+int cr_topk_merge(const float* d_dist_parts, const int64_t* d_id_parts, uint32_t n_parts,
+                  uint32_t n_queries, uint32_t k, int metric, float* d_out_dist,
+                  int64_t* d_out_ids, cr_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CU_ROARING_B200_H */
