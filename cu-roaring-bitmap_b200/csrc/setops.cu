@@ -46,6 +46,7 @@ enum { MODE_AND_SUB = 0, MODE_OR = 1, MODE_XOR = 2 };
 struct Operands {
   DevBitmap op[kMaxOperands];
   uint32_t np, nn, mode, n_keys;
+  uint32_t res_max_key;  // keys above it (IDs beyond the universe) are an error
 };
 
 // Per-key decision. Returns false when the key produces no work item.
@@ -105,6 +106,7 @@ __device__ __forceinline__ bool plan_key(const Operands& ops, uint32_t key, KeyP
 struct WorkTotals {
   uint32_t n, nb;
   unsigned long long ab, rb;
+  uint32_t err, pad;
 };
 
 __global__ void __launch_bounds__(kTile) k_plan_tiles(const Operands* __restrict__ ops_p,
@@ -150,6 +152,7 @@ __global__ void __launch_bounds__(kTile) k_plan_work(const Operands* __restrict_
   const unsigned long long bs = block_exclusive_scan<kTile, unsigned long long>(has && kp.type == kBitmap, s_red, &tot);
   const unsigned long long ao = block_exclusive_scan<kTile, unsigned long long>(has && kp.type == kArray ? kp.bound : 0u, s_red, &tot);
   const unsigned long long ro = block_exclusive_scan<kTile, unsigned long long>(has && kp.type == kRun ? kp.bound : 0u, s_red, &tot);
+  if (has && key > ops.res_max_key) atomicOr(&header->err, 1u);
   if (has) {
     uint32_t off;
     if (kp.type == kBitmap) off = static_cast<uint32_t>((s_base.nb + bs) * kBitmapBytes);
@@ -158,7 +161,12 @@ __global__ void __launch_bounds__(kTile) k_plan_work(const Operands* __restrict_
     work[s_base.n + wi] = make_uint4(key | (uint32_t(kp.type) << 16) | (uint32_t(kp.copy) << 24), off,
                                      kp.src, static_cast<uint32_t>(kp.src_idx));
   }
-  if (blockIdx.x == 0 && threadIdx.x == 0) *header = s_all;
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    header->n = s_all.n;
+    header->nb = s_all.nb;
+    header->ab = s_all.ab;
+    header->rb = s_all.rb;
+  }
 }
 
 __device__ __forceinline__ void store4(uint64_t* dst, const uint64_t w[4])
@@ -413,6 +421,8 @@ void kway(const std::vector<const cr_gpu_roaring*>& P, const std::vector<const c
   if (mode == MODE_AND_SUB && any_p_empty) return;
   const uint32_t K = max_key + 1;
   h_ops.n_keys = K;
+  h_ops.res_max_key = max_key_for(U);
+  max_key = max_key_for(U);
   const uint32_t n_tiles = div_up(K, kTile);
 
   // scratch: operands | work | counts | dst_off | plan tiles | final tiles | headers
@@ -431,12 +441,14 @@ void kway(const std::vector<const cr_gpu_roaring*>& P, const std::vector<const c
   WorkTotals* d_hdr = reinterpret_cast<WorkTotals*>(p);
 
   CR_CUDA(cudaMemcpyAsync(d_ops, &h_ops, sizeof(Operands), cudaMemcpyHostToDevice, s));
+  CR_CUDA(cudaMemsetAsync(d_hdr, 0, sizeof(WorkTotals), s));
   k_plan_tiles<<<n_tiles, kTile, 0, s>>>(d_ops, tiles);
   k_plan_work<<<n_tiles, kTile, 0, s>>>(d_ops, tiles, n_tiles, work, d_hdr);
   CR_CUDA(cudaGetLastError());
   WorkTotals h{};
   CR_CUDA(cudaMemcpyAsync(&h, d_hdr, sizeof(h), cudaMemcpyDeviceToHost, s));
   CR_CUDA(cudaStreamSynchronize(s));  // sync 1: the work list size
+  if (h.err) fail(CR_ERR_RANGE, "set operation: an operand holds IDs beyond the result universe");
   if (h.n == 0) return;
 
   cr_gpu_roaring blk{};

@@ -39,14 +39,17 @@ __device__ __forceinline__ bool warp_contains(const GpuRoaringView& r, uint32_t 
       }
     }
   }
-  idx = __shfl_sync(active, idx, leader);
+  // Every lane of `active` takes part in all three broadcasts before any
+  // lane branches on the result: a __shfl_sync whose mask names a lane that
+  // has already returned is undefined (it faults on sm_100).
+  idx      = __shfl_sync(active, idx, leader);
+  meta_off = __shfl_sync(active, meta_off, leader);
+  meta_tc  = __shfl_sync(active, meta_tc, leader);
   if (idx < 0) return r.negated;
   if (r.all_bitmap) {
     const uint64_t w = __ldg(r.bitmap_data + (static_cast<size_t>(idx) << 10) + (low >> 6));
     return static_cast<bool>((w >> (low & 63u)) & 1u) != r.negated;
   }
-  meta_off = __shfl_sync(active, meta_off, leader);
-  meta_tc  = __shfl_sync(active, meta_tc, leader);
   const bool hit = r.contains_in(static_cast<ContainerTypeD>(meta_tc & 0xFFu), meta_off,
                                  static_cast<uint16_t>(meta_tc >> 8), low);
   return hit != r.negated;

@@ -1,0 +1,188 @@
+// C++ drop-in test: a user program written against the reference's public
+// C++ API (cu_roaring::upload_from_ids, set_operation, multi_and,
+// decompress_to_bitset, enumerate_ids, make_view + GpuRoaringView::contains /
+// warp_contains inside user kernels), compiled against this engine's headers
+// and linked to libcuroaring_b200.so. Cases follow the reference's
+// test/test_promote.cu, test/test_complement.cu, test/test_device_query.cu and
+// test/test_decompress.cu. Prints one line per check and exits non-zero on
+// any failure.
+#include <algorithm>
+#include <cstdio>
+#include <random>
+#include <set>
+#include <vector>
+
+#include "cu_roaring/cu_roaring.cuh"
+
+static int g_fail = 0, g_pass = 0;
+#define EXPECT(cond, msg)                                   \
+  do {                                                      \
+    if (cond) { ++g_pass; }                                 \
+    else { ++g_fail; std::printf("FAIL %s (%s:%d)\n", msg, __FILE__, __LINE__); } \
+  } while (0)
+
+__global__ void user_contains(cu_roaring::GpuRoaringView v, const uint32_t* q, uint8_t* out, uint32_t n)
+{
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = v.contains(q[i]);
+}
+
+__global__ void user_warp_contains(cu_roaring::GpuRoaringView v, const uint32_t* q, uint8_t* out,
+                                   uint32_t n)
+{
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = cu_roaring::warp_contains(v, q[i]);
+}
+
+static std::vector<uint8_t> query(const cu_roaring::GpuRoaring& bm, const std::vector<uint32_t>& q,
+                                  bool warp)
+{
+  uint32_t* dq = nullptr;
+  uint8_t* dr = nullptr;
+  const uint32_t n = static_cast<uint32_t>(q.size());
+  CUDA_CHECK(cudaMalloc(&dq, n * 4));
+  CUDA_CHECK(cudaMalloc(&dr, n));
+  CUDA_CHECK(cudaMemcpy(dq, q.data(), n * 4, cudaMemcpyHostToDevice));
+  auto v = cu_roaring::make_view(bm);
+  if (warp) user_warp_contains<<<(n + 255) / 256, 256>>>(v, dq, dr, n);
+  else user_contains<<<(n + 255) / 256, 256>>>(v, dq, dr, n);
+  CUDA_CHECK(cudaGetLastError());
+  std::vector<uint8_t> r(n);
+  CUDA_CHECK(cudaMemcpy(r.data(), dr, n, cudaMemcpyDeviceToHost));
+  cudaFree(dq);
+  cudaFree(dr);
+  return r;
+}
+
+static std::vector<uint32_t> to_host_bitset(const cu_roaring::GpuRoaring& bm)
+{
+  const uint32_t words = (bm.universe_size + 31) / 32;
+  std::vector<uint32_t> h(words);
+  if (!words) return h;
+  uint32_t* d = cu_roaring::decompress_to_bitset(bm);
+  CUDA_CHECK(cudaDeviceSynchronize());
+  CUDA_CHECK(cudaMemcpy(h.data(), d, words * 4, cudaMemcpyDeviceToHost));
+  cudaFree(d);
+  return h;
+}
+
+static void check_against(const cu_roaring::GpuRoaring& bm, const std::vector<bool>& truth,
+                          const std::vector<uint32_t>& q, const char* what)
+{
+  for (int warp = 0; warp < 2; ++warp) {
+    auto r = query(bm, q, warp);
+    bool ok = true;
+    for (size_t i = 0; i < q.size(); ++i)
+      ok &= (r[i] != 0) == (q[i] < truth.size() && truth[q[i]]);
+    EXPECT(ok, what);
+  }
+}
+
+int main()
+{
+  using namespace cu_roaring;
+  {  // test/test_promote.cu:387-416
+    std::vector<uint32_t> ids = {200, 5, 100000, 42, 65536, 0, 100000, 5};
+    auto bm = upload_from_ids(ids.data(), ids.size(), 200000, 0, PROMOTE_KEEP_DEFAULT);
+    EXPECT(bm.total_cardinality == 6, "unsorted: cardinality 6");
+    std::vector<bool> t(200000, false);
+    for (auto i : ids) t[i] = true;
+    check_against(bm, t, {0, 5, 42, 200, 65536, 100000, 1, 100, 65535}, "unsorted: membership");
+    gpu_roaring_free(bm);
+  }
+  {  // test/test_complement.cu:129-150 (U=10, 90%)
+    std::vector<uint32_t> ids = {0, 1, 2, 3, 4, 5, 6, 8, 9};
+    auto bm = upload_from_ids(ids.data(), ids.size(), 10);
+    EXPECT(bm.negated, "complement: negated");
+    std::vector<bool> t(10, false);
+    for (auto i : ids) t[i] = true;
+    std::vector<uint32_t> q(10);
+    for (uint32_t i = 0; i < 10; ++i) q[i] = i;
+    check_against(bm, t, q, "complement: contains");
+    // NOT({7}) AND {4,6,7} = {4,6}  (test/test_complement.cu:320-353)
+    std::vector<uint32_t> bids = {4, 6, 7};
+    auto b = upload_from_ids(bids.data(), 3, 10);
+    auto r = set_operation(bm, b, SetOp::AND);
+    EXPECT(r.total_cardinality == 2, "user example: cardinality");
+    int64_t* d = enumerate_ids(r);
+    int64_t h[2] = {0, 0};
+    CUDA_CHECK(cudaDeviceSynchronize());
+    CUDA_CHECK(cudaMemcpy(h, d, 16, cudaMemcpyDeviceToHost));
+    EXPECT(h[0] == 4 && h[1] == 6, "user example: {4,6}");
+    cudaFree(d);
+    gpu_roaring_free(r);
+    gpu_roaring_free(b);
+    gpu_roaring_free(bm);
+  }
+  {  // test/test_device_query.cu:83-99 dense random, queries i*20; promoted too
+    std::mt19937 gen(42);
+    std::uniform_real_distribution<double> dist(0.0, 1.0);
+    std::vector<uint32_t> ids;
+    std::vector<bool> t(200000, false);
+    for (uint32_t i = 0; i < 200000; ++i)
+      if (dist(gen) < 0.5) { ids.push_back(i); t[i] = true; }
+    std::vector<uint32_t> q;
+    for (uint32_t i = 0; i < 10000; ++i) q.push_back(i * 20);
+    for (uint32_t thr : {PROMOTE_KEEP_DEFAULT, PROMOTE_ALL}) {
+      auto bm = upload_from_ids(ids.data(), ids.size(), 200000, 0, thr);
+      check_against(bm, t, q, "dense random: contains / warp_contains");
+      auto p = promote_to_bitmap(bm);
+      CUDA_CHECK(cudaDeviceSynchronize());
+      check_against(p, t, q, "promoted: contains");
+      EXPECT(to_host_bitset(p) == to_host_bitset(bm), "promote keeps the set");
+      auto c = gpu_roaring_deep_copy(bm);
+      CUDA_CHECK(cudaDeviceSynchronize());
+      EXPECT(to_host_bitset(c) == to_host_bitset(bm), "deep copy keeps the set");
+      gpu_roaring_free(c);
+      gpu_roaring_free(p);
+      gpu_roaring_free(bm);
+    }
+  }
+  {  // test/test_device_query.cu:137-169 clustered + run containers
+    std::vector<uint32_t> ids;
+    std::vector<bool> t(200000, false);
+    for (uint32_t i = 1000; i <= 5000; ++i) { ids.push_back(i); t[i] = true; }
+    for (uint32_t i = 70000; i <= 80000; ++i) { ids.push_back(i); t[i] = true; }
+    auto bm = upload_from_ids(ids.data(), ids.size(), 200000, 0, PROMOTE_KEEP_DEFAULT);
+    EXPECT(bm.n_run_containers == 1 && bm.n_array_containers == 1, "runs: container types");
+    std::vector<uint32_t> q;
+    for (uint32_t i = 0; i < 100000; i += 3) q.push_back(i);
+    check_against(bm, t, q, "runs: contains");
+    gpu_roaring_free(bm);
+  }
+  {  // multi_and with a negated input (test/test_complement.cu:503-545)
+    std::mt19937 gen(42);
+    std::vector<uint32_t> a, b, c;
+    std::vector<bool> t(50000, false);
+    std::vector<bool> ta(50000), tb(50000), tc(50000);
+    for (uint32_t i = 0; i < 50000; ++i) {
+      if (gen() % 3 == 0) { a.push_back(i); ta[i] = true; }
+      if (gen() % 2 == 0) { b.push_back(i); tb[i] = true; }
+      if (gen() % 4 != 0) { c.push_back(i); tc[i] = true; }
+      t[i] = ta[i] && tb[i] && tc[i];
+    }
+    GpuRoaring in[3] = {upload_from_ids(a.data(), a.size(), 50000),
+                        upload_from_ids(b.data(), b.size(), 50000),
+                        upload_from_ids(c.data(), c.size(), 50000)};
+    EXPECT(in[2].negated, "multi_and: third input negated");
+    auto r = multi_and(in, 3);
+    std::vector<uint32_t> q(50000);
+    for (uint32_t i = 0; i < 50000; ++i) q[i] = i;
+    check_against(r, t, q, "multi_and with negation");
+    gpu_roaring_free(r);
+    for (auto& x : in) gpu_roaring_free(x);
+  }
+  {  // error convention: an ID outside the universe throws std::runtime_error
+    std::vector<uint32_t> ids = {5, 500};
+    bool threw = false;
+    try {
+      auto bm = upload_from_ids(ids.data(), 2, 100);
+      gpu_roaring_free(bm);
+    } catch (const std::runtime_error&) {
+      threw = true;
+    }
+    EXPECT(threw, "out-of-universe ID throws");
+  }
+  std::printf("api_test: %d passed, %d failed\n", g_pass, g_fail);
+  return g_fail ? 1 : 0;
+}
