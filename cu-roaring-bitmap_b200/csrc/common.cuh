@@ -138,6 +138,15 @@ struct DevBitmap {
 // assembled by other code) a full 65536-entry index is built into `holder`.
 DevBitmap make_dev(const cr_gpu_roaring* b, Scratch& holder, cudaStream_t s);
 
+// Optional CUDA-event bracketing of the dominant kernels (cr_profile_enable).
+struct ProfileScope {
+  int kind;
+  cudaStream_t s;
+  bool on;
+  ProfileScope(int k, cudaStream_t st);
+  ~ProfileScope();
+};
+
 // ------------------------------------------------------- block primitives
 // Exclusive scan over a block of BLOCK threads (multiple of 32). Returns the
 // exclusive prefix; *total gets the block sum. `smem` holds BLOCK/32 values.

@@ -183,9 +183,53 @@ DevBitmap make_dev(const cr_gpu_roaring* b, Scratch& holder, cudaStream_t s)
   return d;
 }
 
+namespace {
+constexpr int kProfileKinds = 8;
+bool g_profile = false;
+struct ProfileEvents {
+  cudaEvent_t start[kProfileKinds] = {};
+  cudaEvent_t stop[kProfileKinds] = {};
+  bool used[kProfileKinds] = {};
+};
+thread_local ProfileEvents g_prof;
+}  // namespace
+
+ProfileScope::ProfileScope(int k, cudaStream_t st) : kind(k), s(st), on(g_profile)
+{
+  if (!on || kind < 0 || kind >= kProfileKinds) { on = false; return; }
+  if (!g_prof.start[kind]) {
+    CR_CUDA(cudaEventCreate(&g_prof.start[kind]));
+    CR_CUDA(cudaEventCreate(&g_prof.stop[kind]));
+  }
+  CR_CUDA(cudaEventRecord(g_prof.start[kind], s));
+}
+
+ProfileScope::~ProfileScope()
+{
+  if (!on) return;
+  cudaEventRecord(g_prof.stop[kind], s);
+  g_prof.used[kind] = true;
+}
+
 }  // namespace crb
 
 using namespace crb;
+
+extern "C" int cr_profile_enable(int on)
+{
+  g_profile = on != 0;
+  return CR_OK;
+}
+
+extern "C" int cr_profile_last_ms(int kernel, float* ms)
+{
+  CR_API_BEGIN
+  CR_REQUIRE(ms != nullptr && kernel >= 0 && kernel < kProfileKinds, "cr_profile_last_ms: bad argument");
+  CR_REQUIRE(g_prof.used[kernel], "cr_profile_last_ms: no profiled launch of this kernel");
+  CR_CUDA(cudaEventSynchronize(g_prof.stop[kernel]));
+  CR_CUDA(cudaEventElapsedTime(ms, g_prof.start[kernel], g_prof.stop[kernel]));
+  CR_API_END
+}
 
 extern "C" const char* cr_last_error_string(void) { return g_last_error.c_str(); }
 

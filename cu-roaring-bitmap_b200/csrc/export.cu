@@ -47,8 +47,9 @@ __global__ void __launch_bounds__(256) k_contains(cu_roaring::GpuRoaringView v,
     }
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u) {
-      bool hit = false;
-      if (in[u]) hit = MODE ? cu_roaring::warp_contains(v, id[u]) : v.contains(id[u]);
+      // Every lane calls the query (tail lanes on a dummy ID, result masked):
+      // warp_contains is warp-synchronous and must not sit in a lane branch.
+      const bool hit = (MODE ? cu_roaring::warp_contains(v, id[u]) : v.contains(id[u])) && in[u];
       const uint32_t bits = __ballot_sync(0xFFFFFFFFu, hit);
       if (lane == 0 && w0 + u < n_words) __stcs(out + w0 + u, bits);
     }
@@ -258,6 +259,7 @@ extern "C" int cr_contains_batch(const cr_gpu_roaring* bm, const uint32_t* d_ids
   const uint64_t words = (n + 31) / 32;
   const uint64_t want = (words + 8 * kUnroll - 1) / (8 * kUnroll);
   const int grid = static_cast<int>(std::max<uint64_t>(1, std::min<uint64_t>(want, uint64_t(sm_count()) * 8)));
+  ProfileScope prof(CR_KERNEL_CONTAINS, s);
   if (mode) k_contains<1><<<grid, 256, 0, s>>>(v, d_ids, n, d_out_bits);
   else k_contains<0><<<grid, 256, 0, s>>>(v, d_ids, n, d_out_bits);
   CR_CUDA(cudaGetLastError());
@@ -274,6 +276,7 @@ extern "C" int cr_decompress_to_bitset(const cr_gpu_roaring* bm, uint32_t* d_out
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   Scratch holder;
   const DevBitmap b = make_dev(bm, holder, s);
+  ProfileScope prof(CR_KERNEL_DECOMPRESS, s);
   k_decompress<<<div_up(output_words, kChunkWords32), 256, 0, s>>>(b, d_output, output_words);
   CR_CUDA(cudaGetLastError());
   CR_API_END

@@ -460,7 +460,10 @@ void kway(const std::vector<const cr_gpu_roaring*>& P, const std::vector<const c
   blk.max_key = max_key;
   alloc_result(&blk, s);
   Scratch arr(h.ab, s);
-  k_execute<<<h.n, 256, 0, s>>>(d_ops, work, blk, arr.as<uint16_t>(), counts);
+  {
+    ProfileScope prof(CR_KERNEL_SETOP, s);
+    k_execute<<<h.n, 256, 0, s>>>(d_ops, work, blk, arr.as<uint16_t>(), counts);
+  }
   const uint32_t f_tiles = div_up(h.n, kTile);
   k_final_tiles<<<f_tiles, kTile, 0, s>>>(work, counts, h.n, d_ops, ftiles);
   CR_CUDA(cudaGetLastError());

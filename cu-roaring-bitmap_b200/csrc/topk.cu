@@ -1,21 +1,554 @@
-// placeholder, replaced by the tcgen05 implementation
-#include "common.cuh"
+// cu_roaring B200 engine — fused filtered brute-force top-k.
+//
+// No reference counterpart (the reference only describes feeding
+// enumerate_ids into an external SDDMM, README.md:265-285). One kernel per
+// (128-query tile, database slice):
+//
+//   warp 0  TMA producer: the query tile once (A operand, 32 KiB), then
+//           database tiles of 256 rows x 128 dims (B operand, 64 KiB) into a
+//           2-stage ring, both as 128-byte-swizzled K-major tiles.
+//   warp 1  one elected thread issues 8 tcgen05.mma (M=128 queries,
+//           N=256 rows, K=16 each, fp16 in, fp32 accumulate) per tile into
+//           one of two 256-column TMEM accumulators, then tcgen05.commit
+//           frees the smem stage and signals the epilogue.
+//   warps 2-5  epilogue, one thread per query (TMEM lane): for each 32-row
+//           chunk the filter word (one u32 of the shard's pass bitset) is
+//           read first; chunks with no passing row are never loaded from
+//           TMEM; passing scores are compared with the thread's running k-th
+//           best and rare survivors go to a 32-entry shared-memory buffer,
+//           merged into a per-thread sorted top-k list when full.
+//
+// A second kernel merges the per-slice lists of each query (bitonic sort in
+// shared memory) and converts internal scores to distances. Internal score
+// is "larger is better": IP -> q.x; L2 -> 2 q.x - |x|^2 (distance
+// |q|^2 - score). Ties are broken toward the smaller row id.
+#include <cuda.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "chunk_ops.cuh"
+#include "cu_roaring/device/make_view.cuh"
+#include "cu_roaring/device/roaring_warp_query.cuh"
+#include "tcgen05.cuh"
+
+namespace crb {
+namespace {
+
+using namespace sm100;
+
+constexpr uint32_t BM = 128;       // queries per CTA (UMMA M, TMEM lanes)
+constexpr uint32_t BN = 256;       // database rows per tile (UMMA N)
+constexpr uint32_t DIM = 128;      // K
+constexpr uint32_t STAGES = 2;
+constexpr uint32_t BUF = 32;       // candidate buffer entries per query
+constexpr uint32_t THREADS = 192;  // 6 warps
+constexpr uint32_t KB_BYTES_Q = BM * 128;    // one 64-dim K-block of the query tile
+constexpr uint32_t KB_BYTES_DB = BN * 128;   // one 64-dim K-block of a database tile
+constexpr uint32_t STAGE_BYTES = 2 * KB_BYTES_DB;
+constexpr uint32_t SMEM_Q = 0;
+constexpr uint32_t SMEM_DB = SMEM_Q + 2 * KB_BYTES_Q;
+constexpr uint32_t SMEM_BUF_S = SMEM_DB + STAGES * STAGE_BYTES;
+constexpr uint32_t SMEM_BUF_R = SMEM_BUF_S + BUF * BM * 4;
+constexpr uint32_t SMEM_BAR = SMEM_BUF_R + BUF * BM * 4;
+constexpr uint32_t SMEM_TOTAL = SMEM_BAR + 128 + 1024;  // + alignment slack
+constexpr uint32_t TMEM_COLS = 512;                     // two 256-column accumulators
+constexpr uint32_t kIdesc = idesc_f16_f32(BM, BN);
+
+struct TopkParams {
+  uint32_t n_rows, n_queries, k, metric;
+  uint32_t n_tiles, tiles_per_slice;
+  const uint32_t* pass;  // local pass bitset, null = every row passes
+  const float* norms;    // squared row norms (L2)
+  float* list_s;         // per-thread sorted lists: [cta][2][k][BM]
+  uint32_t* list_r;
+  float* part_s;         // [slice][Q][k] internal scores
+  int64_t* part_id;
+  uint64_t row_offset;
+  uint32_t* err;
+};
+
+__device__ __forceinline__ bool better(float as, uint32_t ar, float bs, uint32_t br)
+{
+  return as > bs || (as == bs && ar < br);
+}
+
+// Merges this thread's nb buffered candidates into its sorted list.
+__device__ void flush_buffer(float* bs, uint32_t* br, uint32_t nb, uint32_t t, float* Ls,
+                             uint32_t* Lr, uint32_t k, uint32_t& half, uint32_t& cnt,
+                             float& thr_s, uint32_t& thr_r)
+{
+  for (uint32_t i = 1; i < nb; ++i) {  // insertion sort, best first
+    const float s = bs[i * BM + t];
+    const uint32_t r = br[i * BM + t];
+    uint32_t j = i;
+    while (j > 0 && better(s, r, bs[(j - 1) * BM + t], br[(j - 1) * BM + t])) {
+      bs[j * BM + t] = bs[(j - 1) * BM + t];
+      br[j * BM + t] = br[(j - 1) * BM + t];
+      --j;
+    }
+    bs[j * BM + t] = s;
+    br[j * BM + t] = r;
+  }
+  const uint32_t src = half, dst = half ^ 1u;
+  uint32_t i = 0, j = 0, o = 0;
+  while (o < k && (i < cnt || j < nb)) {
+    const size_t si = (size_t(src) * k + i) * BM + t;
+    bool take_list;
+    if (i >= cnt) take_list = false;
+    else if (j >= nb) take_list = true;
+    else take_list = better(Ls[si], Lr[si], bs[j * BM + t], br[j * BM + t]);
+    const size_t so = (size_t(dst) * k + o) * BM + t;
+    if (take_list) { Ls[so] = Ls[si]; Lr[so] = Lr[si]; ++i; }
+    else { Ls[so] = bs[j * BM + t]; Lr[so] = br[j * BM + t]; ++j; }
+    ++o;
+  }
+  cnt = o;
+  half = dst;
+  if (cnt == k) {
+    const size_t sl = (size_t(dst) * k + k - 1) * BM + t;
+    thr_s = Ls[sl];
+    thr_r = Lr[sl];
+  }
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    k_topk(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tdb,
+           TopkParams p)
+{
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sQ = smem + SMEM_Q;
+  uint8_t* sDB = smem + SMEM_DB;
+  float* buf_s = reinterpret_cast<float*>(smem + SMEM_BUF_S);
+  uint32_t* buf_r = reinterpret_cast<uint32_t*>(smem + SMEM_BUF_R);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SMEM_BAR);
+  uint64_t* q_full = bars + 0;
+  uint64_t* full = bars + 1;       // [STAGES]
+  uint64_t* empty = bars + 3;      // [STAGES]
+  uint64_t* acc_full = bars + 5;   // [2]
+  uint64_t* acc_empty = bars + 7;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
+
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t qt = blockIdx.x, slice = blockIdx.y;
+  const uint32_t t0 = slice * p.tiles_per_slice;
+  const uint32_t t1 = min(p.n_tiles, t0 + p.tiles_per_slice);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (uint32_t s = 0; s < STAGES; ++s) { mbar_init(full + s, 1); mbar_init(empty + s, 1); }
+    for (uint32_t a = 0; a < 2; ++a) { mbar_init(acc_full + a, 1); mbar_init(acc_empty + a, 4); }
+    fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc(tmem_slot, TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer
+    if (lane == 0) {
+      prefetch_tmap(&tq);
+      prefetch_tmap(&tdb);
+      mbar_expect_tx(q_full, 2 * KB_BYTES_Q);
+      tma_load_2d(&tq, q_full, sQ, 0, int32_t(qt * BM));
+      tma_load_2d(&tq, q_full, sQ + KB_BYTES_Q, 64, int32_t(qt * BM));
+      for (uint32_t t = t0; t < t1; ++t) {
+        const uint32_t it = t - t0, s = it % STAGES;
+        if (!mbar_wait(empty + s, ((it / STAGES) & 1u) ^ 1u, p.err, 1u)) break;
+        uint8_t* dst = sDB + s * STAGE_BYTES;
+        mbar_expect_tx(full + s, STAGE_BYTES);
+        tma_load_2d(&tdb, full + s, dst, 0, int32_t(t * BN));
+        tma_load_2d(&tdb, full + s, dst + KB_BYTES_DB, 64, int32_t(t * BN));
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- UMMA issuer
+    if (lane == 0) {
+      bool ok = mbar_wait(q_full, 0, p.err, 2u);
+      const uint32_t aq = smem_addr(sQ);
+      for (uint32_t t = t0; t < t1 && ok; ++t) {
+        const uint32_t it = t - t0, s = it % STAGES, a = it & 1u;
+        if (!mbar_wait(full + s, (it / STAGES) & 1u, p.err, 4u)) break;
+        if (!mbar_wait(acc_empty + a, ((it >> 1) & 1u) ^ 1u, p.err, 8u)) break;
+        tc_fence_after();
+        const uint32_t adb = smem_addr(sDB + s * STAGE_BYTES);
+#pragma unroll
+        for (uint32_t kk = 0; kk < DIM / 16; ++kk) {
+          const uint32_t kb = kk >> 2, ko = (kk & 3u) * 32u;  // K-block, byte offset in 128-B row
+          const uint64_t ad = smem_desc_sw128(aq + kb * KB_BYTES_Q + ko);
+          const uint64_t bd = smem_desc_sw128(adb + kb * KB_BYTES_DB + ko);
+          umma_f16(tmem + a * BN, ad, bd, kIdesc, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(empty + s);
+        umma_commit(acc_full + a);
+      }
+    }
+  } else {
+    // ---------------- epilogue: warps 2..5, one thread per query
+    const uint32_t quarter = warp & 3u;               // TMEM lane quarter this warp may access
+    const uint32_t t_local = quarter * 32 + lane;     // query row inside the tile
+    const uint32_t qi = qt * BM + t_local;
+    const bool valid_q = qi < p.n_queries;
+    const size_t cta = size_t(slice) * gridDim.x + qt;
+    float* Ls = p.list_s + cta * 2 * p.k * BM;
+    uint32_t* Lr = p.list_r + cta * 2 * p.k * BM;
+    uint32_t half = 0, cnt = 0, nb = 0, thr_r = 0xFFFFFFFFu;
+    float thr_s = -INFINITY;
+    const bool l2 = p.metric == CR_METRIC_L2;
+    for (uint32_t t = t0; t < t1; ++t) {
+      const uint32_t it = t - t0, a = it & 1u;
+      if (!mbar_wait(acc_full + a, (it >> 1) & 1u, p.err, 16u)) break;
+      tc_fence_after();
+      const uint32_t row0 = t * BN;
+#pragma unroll 1
+      for (uint32_t c = 0; c < BN / 32; ++c) {
+        const uint32_t r0 = row0 + c * 32;
+        if (r0 >= p.n_rows) break;
+        uint32_t m = p.pass ? __ldg(p.pass + (r0 >> 5)) : 0xFFFFFFFFu;
+        const uint32_t left = p.n_rows - r0;
+        if (left < 32) m &= (1u << left) - 1u;
+        if (m == 0) continue;
+        float v[32];
+        tmem_ld32(tmem + ((quarter * 32u) << 16) + a * BN + c * 32, v);
+        if (!valid_q) continue;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          if (!((m >> j) & 1u)) continue;
+          const uint32_t r = r0 + j;
+          const float sc = l2 ? 2.f * v[j] - __ldg(p.norms + r) : v[j];
+          if (better(sc, r, thr_s, thr_r)) {
+            buf_s[nb * BM + t_local] = sc;
+            buf_r[nb * BM + t_local] = r;
+            if (++nb == BUF) {
+              flush_buffer(buf_s, buf_r, nb, t_local, Ls, Lr, p.k, half, cnt, thr_s, thr_r);
+              nb = 0;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty + a);
+    }
+    if (valid_q) {
+      if (nb) flush_buffer(buf_s, buf_r, nb, t_local, Ls, Lr, p.k, half, cnt, thr_s, thr_r);
+      const size_t base = (size_t(slice) * p.n_queries + qi) * p.k;
+      for (uint32_t i = 0; i < p.k; ++i) {
+        const size_t si = (size_t(half) * p.k + i) * BM + t_local;
+        p.part_s[base + i] = i < cnt ? Ls[si] : -INFINITY;
+        p.part_id[base + i] = i < cnt ? int64_t(Lr[si]) + int64_t(p.row_offset) : int64_t(-1);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, TMEM_COLS);
+}
+
+// ------------------------------------------------------------------ merge
+constexpr uint32_t MERGE_N = 4096;
+constexpr uint32_t MERGE_THREADS = 512;
+
+__device__ __forceinline__ bool better64(float as, int64_t ai, float bs, int64_t bi)
+{
+  // Valid ids before padding (-1 sorts last on ties at -inf).
+  const uint64_t ua = static_cast<uint64_t>(ai), ub = static_cast<uint64_t>(bi);
+  return as > bs || (as == bs && ua < ub);
+}
+
+__device__ void bitonic_sort(float* s, int64_t* id)
+{
+  for (uint32_t size = 2; size <= MERGE_N; size <<= 1) {
+    for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
+      for (uint32_t pr = threadIdx.x; pr < MERGE_N / 2; pr += MERGE_THREADS) {
+        const uint32_t i = (pr / stride) * 2 * stride + (pr % stride), j = i + stride;
+        const bool first_better = better64(s[i], id[i], s[j], id[j]);
+        const bool want_first_better = (i & size) == 0;
+        if (first_better != want_first_better) {
+          const float ts = s[i]; s[i] = s[j]; s[j] = ts;
+          const int64_t ti = id[i]; id[i] = id[j]; id[j] = ti;
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
+// One CTA per query: the best k of `parts` sorted lists. kind 0: inputs are
+// internal scores of k_topk; kind 1: inputs are final distances.
+__global__ void __launch_bounds__(MERGE_THREADS) k_merge(const float* part_s, const int64_t* part_id,
+                                                         uint32_t parts, uint32_t n_queries,
+                                                         uint32_t k, int metric, int kind,
+                                                         const __half* queries, uint32_t dim,
+                                                         float* out_d, int64_t* out_id)
+{
+  extern __shared__ uint8_t smem_raw[];
+  float* s = reinterpret_cast<float*>(smem_raw);
+  int64_t* id = reinterpret_cast<int64_t*>(smem_raw + MERGE_N * 4);
+  __shared__ float s_qn;
+  const uint32_t q = blockIdx.x;
+  const bool l2 = metric == CR_METRIC_L2;
+  if (threadIdx.x < 32) {
+    float acc = 0.f;
+    if (l2 && kind == 0)
+      for (uint32_t d = threadIdx.x; d < dim; d += 32) {
+        const float x = __half2float(queries[size_t(q) * dim + d]);
+        acc += x * x;
+      }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
+    if (threadIdx.x == 0) s_qn = acc;
+  }
+  const uint64_t total = uint64_t(parts) * k;
+  auto load = [&](uint64_t c, uint32_t slot) {
+    float v = -INFINITY;
+    int64_t i = -1;
+    if (c < total) {
+      const uint32_t pidx = static_cast<uint32_t>(c / k), e = static_cast<uint32_t>(c % k);
+      const size_t g = (size_t(pidx) * n_queries + q) * k + e;
+      i = part_id[g];
+      const float x = part_s[g];
+      v = (i < 0) ? -INFINITY : (kind == 0 ? x : (l2 ? -x : x));
+    }
+    s[slot] = v;
+    id[slot] = i;
+  };
+  uint64_t pos = 0;
+  for (uint32_t i = threadIdx.x; i < MERGE_N; i += MERGE_THREADS) load(pos + i, i);
+  pos += MERGE_N;
+  __syncthreads();
+  bitonic_sort(s, id);
+  while (pos < total) {
+    for (uint32_t i = k + threadIdx.x; i < MERGE_N; i += MERGE_THREADS) load(pos + (i - k), i);
+    pos += MERGE_N - k;
+    __syncthreads();
+    bitonic_sort(s, id);
+  }
+  const float qn = s_qn;
+  for (uint32_t i = threadIdx.x; i < k; i += MERGE_THREADS) {
+    const int64_t r = id[i];
+    float d;
+    if (r < 0) d = l2 ? INFINITY : -INFINITY;
+    else if (!l2) d = s[i];
+    else d = (kind == 0) ? qn - s[i] : -s[i];
+    out_d[size_t(q) * k + i] = d;
+    out_id[size_t(q) * k + i] = r;
+  }
+}
+
+// Shard-local pass bitset: bit i of word w = filter.contains(row_offset + 32w + i).
+__global__ void k_pass_bits(cu_roaring::GpuRoaringView v, uint64_t row_offset, uint64_t n_rows,
+                            uint32_t* out, uint64_t n_words)
+{
+  const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
+  for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n_words * 32; i += stride) {
+    const uint64_t id = row_offset + i;
+    const bool ok = i < n_rows && id <= 0xFFFFFFFFull;
+    const bool hit = cu_roaring::warp_contains(v, ok ? uint32_t(id) : 0u) && ok;
+    const uint32_t bits = __ballot_sync(0xFFFFFFFFu, hit);
+    if ((threadIdx.x & 31) == 0) out[i >> 5] = bits;
+  }
+}
+
+// Squared norms, 16 lanes per 128-dim row (16 bytes each).
+__global__ void k_row_norms(const uint4* db, uint64_t n_rows, float* out)
+{
+  const uint64_t g = (uint64_t(blockIdx.x) * blockDim.x + threadIdx.x);
+  const uint64_t row = g >> 4;
+  const uint32_t sub = threadIdx.x & 15;
+  float acc = 0.f;
+  if (row < n_rows) {
+    const uint4 x = __ldcs(db + row * 16 + sub);
+    const __half2* h = reinterpret_cast<const __half2*>(&x);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __half22float2(h[i]);
+      acc += f.x * f.x + f.y * f.y;
+    }
+  }
+#pragma unroll
+  for (int o = 8; o; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
+  if (row < n_rows && sub == 0) out[row] = acc;
+}
+
+// ------------------------------------------------------------------- host
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn()
+{
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  if (!fn) fail(CR_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
+  return fn;
+}
+
+// Row-major fp16 matrix [rows x 128] as 2-D tiles of 64 dims x box_rows,
+// 128-byte swizzle (the layout the UMMA descriptors expect).
+CUtensorMap make_map(const void* base, uint64_t rows, uint32_t box_rows)
+{
+  CUtensorMap m;
+  const cuuint64_t dims[2] = {DIM, rows};
+  const cuuint64_t strides[1] = {DIM * 2};
+  const cuuint32_t box[2] = {64, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims,
+                                 strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                 CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) fail(CR_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string(int(r)));
+  return m;
+}
+
+void merge_launch(const float* ps, const int64_t* pid, uint32_t parts, uint32_t nq, uint32_t k,
+                  int metric, int kind, const __half* queries, uint32_t dim, float* od, int64_t* oi,
+                  cudaStream_t s)
+{
+  static std::once_flag once;
+  const size_t smem = MERGE_N * 12;
+  std::call_once(once, [&] {
+    cudaFuncSetAttribute(k_merge, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  });
+  k_merge<<<nq, MERGE_THREADS, smem, s>>>(ps, pid, parts, nq, k, metric, kind, queries, dim, od, oi);
+  CR_CUDA(cudaGetLastError());
+}
+
+void row_norms(const uint16_t* db, uint64_t n_rows, float* out, cudaStream_t s)
+{
+  const uint64_t threads = n_rows * 16;
+  k_row_norms<<<div_up(threads, 256), 256, 0, s>>>(reinterpret_cast<const uint4*>(db), n_rows, out);
+  CR_CUDA(cudaGetLastError());
+}
+
+}  // namespace
+}  // namespace crb
+
 using namespace crb;
-extern "C" int cr_filtered_topk(const uint16_t*, const float*, uint64_t, uint32_t, const uint16_t*,
-                                uint32_t, const cr_gpu_roaring*, uint64_t, uint32_t, int, float*,
-                                int64_t*, cr_stream_t)
+
+extern "C" int cr_row_norms(const uint16_t* d_db, uint64_t n_rows, uint32_t dim, float* d_out,
+                            cr_stream_t stream)
 {
-  set_last_error("cr_filtered_topk: not built yet");
-  return CR_ERR_UNSUPPORTED;
+  CR_API_BEGIN
+  CR_REQUIRE(dim == DIM, "cr_row_norms: dim must be 128");
+  CR_REQUIRE(d_db && d_out, "cr_row_norms: null buffer");
+  CR_REQUIRE((reinterpret_cast<uintptr_t>(d_db) & 15u) == 0, "cr_row_norms: db must be 16-byte aligned");
+  if (n_rows) row_norms(d_db, n_rows, d_out, reinterpret_cast<cudaStream_t>(stream));
+  CR_API_END
 }
-extern "C" int cr_row_norms(const uint16_t*, uint64_t, uint32_t, float*, cr_stream_t)
+
+extern "C" int cr_filtered_topk(const uint16_t* d_db, const float* d_db_norms, uint64_t n_rows,
+                                uint32_t dim, const uint16_t* d_queries, uint32_t n_queries,
+                                const cr_gpu_roaring* filter, uint64_t row_offset, uint32_t k,
+                                int metric, float* d_out_dist, int64_t* d_out_ids,
+                                cr_stream_t stream)
 {
-  set_last_error("cr_row_norms: not built yet");
-  return CR_ERR_UNSUPPORTED;
+  CR_API_BEGIN
+  CR_REQUIRE(dim == DIM, "cr_filtered_topk: this build supports dim == 128");
+  CR_REQUIRE(k >= 1 && k <= 256, "cr_filtered_topk: k must be in [1, 256]");
+  CR_REQUIRE(metric == CR_METRIC_IP || metric == CR_METRIC_L2, "cr_filtered_topk: unknown metric");
+  CR_REQUIRE(n_rows >= 1 && n_rows < (1ull << 31), "cr_filtered_topk: n_rows must be in [1, 2^31)");
+  CR_REQUIRE(n_queries >= 1, "cr_filtered_topk: no queries");
+  CR_REQUIRE(d_db && d_queries && d_out_dist && d_out_ids, "cr_filtered_topk: null buffer");
+  CR_REQUIRE((reinterpret_cast<uintptr_t>(d_db) & 15u) == 0 &&
+                 (reinterpret_cast<uintptr_t>(d_queries) & 15u) == 0,
+             "cr_filtered_topk: db and queries must be 16-byte aligned");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaFuncSetAttribute(k_topk, cudaFuncAttributeMaxDynamicSharedMemorySize, int(SMEM_TOTAL));
+  });
+
+  const uint32_t n_tiles = div_up(n_rows, BN);
+  const uint32_t qtiles = div_up(n_queries, BM);
+  const uint32_t want_slices = std::max(1, sm_count() / int(qtiles));
+  const uint32_t tps = div_up(n_tiles, std::min<uint32_t>(want_slices, n_tiles));
+  const uint32_t slices = div_up(n_tiles, tps);
+  const uint64_t pass_words = (n_rows + 31) / 32 + 1;
+  const bool l2 = metric == CR_METRIC_L2;
+
+  const size_t ctas = size_t(qtiles) * slices;
+  const size_t list_b = ctas * 2 * k * BM * 4;
+  const size_t part_b = size_t(slices) * n_queries * k;
+  Scratch scr(list_b * 2 + part_b * 12 + (filter ? pass_words * 4 : 0) +
+                  ((l2 && !d_db_norms) ? n_rows * 4 : 0) + 64 + 256,
+              s);
+  char* p = scr.as<char>();
+  TopkParams tp{};
+  tp.n_rows = static_cast<uint32_t>(n_rows);
+  tp.n_queries = n_queries;
+  tp.k = k;
+  tp.metric = metric;
+  tp.n_tiles = n_tiles;
+  tp.tiles_per_slice = tps;
+  tp.row_offset = row_offset;
+  tp.list_s = reinterpret_cast<float*>(p); p += list_b;
+  tp.list_r = reinterpret_cast<uint32_t*>(p); p += list_b;
+  tp.part_id = reinterpret_cast<int64_t*>(p); p += part_b * 8;
+  tp.part_s = reinterpret_cast<float*>(p); p += part_b * 4;
+  p = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(p) + 15) & ~uintptr_t(15));
+  if (filter) {
+    uint32_t* pass = reinterpret_cast<uint32_t*>(p);
+    p += pass_words * 4;
+    const cu_roaring::GpuRoaringView v =
+        cu_roaring::make_view(*reinterpret_cast<const cu_roaring::GpuRoaring*>(filter));
+    const uint64_t threads = pass_words * 32;
+    const int grid = static_cast<int>(std::min<uint64_t>(div_up(threads, 256), uint64_t(sm_count()) * 16));
+    k_pass_bits<<<grid, 256, 0, s>>>(v, row_offset, n_rows, pass, pass_words);
+    tp.pass = pass;
+  }
+  if (l2) {
+    if (d_db_norms) {
+      tp.norms = d_db_norms;
+    } else {
+      float* nrm = reinterpret_cast<float*>(p);
+      p += n_rows * 4;
+      row_norms(d_db, n_rows, nrm, s);
+      tp.norms = nrm;
+    }
+  }
+  p = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(p) + 15) & ~uintptr_t(15));
+  tp.err = reinterpret_cast<uint32_t*>(p);
+  CR_CUDA(cudaMemsetAsync(tp.err, 0, 4, s));
+  const CUtensorMap tq = make_map(d_queries, n_queries, BM);
+  const CUtensorMap tdb = make_map(d_db, n_rows, BN);
+  {
+    ProfileScope prof(CR_KERNEL_TOPK, s);
+    k_topk<<<dim3(qtiles, slices), THREADS, SMEM_TOTAL, s>>>(tq, tdb, tp);
+  }
+  CR_CUDA(cudaGetLastError());
+  merge_launch(tp.part_s, tp.part_id, slices, n_queries, k, metric, 0,
+               reinterpret_cast<const __half*>(d_queries), dim, d_out_dist, d_out_ids, s);
+  uint32_t h_err = 0;
+  CR_CUDA(cudaMemcpyAsync(&h_err, tp.err, 4, cudaMemcpyDeviceToHost, s));
+  CR_CUDA(cudaStreamSynchronize(s));
+  if (h_err) fail(CR_ERR_DEVICE, "cr_filtered_topk: pipeline wait timed out (code " + std::to_string(h_err) + ")");
+  CR_API_END
 }
-extern "C" int cr_topk_merge(const float*, const int64_t*, uint32_t, uint32_t, uint32_t, int,
-                             float*, int64_t*, cr_stream_t)
+
+extern "C" int cr_topk_merge(const float* d_dist_parts, const int64_t* d_id_parts, uint32_t n_parts,
+                             uint32_t n_queries, uint32_t k, int metric, float* d_out_dist,
+                             int64_t* d_out_ids, cr_stream_t stream)
 {
-  set_last_error("cr_topk_merge: not built yet");
-  return CR_ERR_UNSUPPORTED;
+  CR_API_BEGIN
+  CR_REQUIRE(d_dist_parts && d_id_parts && d_out_dist && d_out_ids, "cr_topk_merge: null buffer");
+  CR_REQUIRE(k >= 1 && k <= 256 && n_parts >= 1, "cr_topk_merge: bad k or n_parts");
+  merge_launch(d_dist_parts, d_id_parts, n_parts, n_queries, k, metric, 1, nullptr, 0, d_out_dist,
+               d_out_ids, reinterpret_cast<cudaStream_t>(stream));
+  CR_API_END
 }

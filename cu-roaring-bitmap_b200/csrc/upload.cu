@@ -503,6 +503,7 @@ static void build_from_chunks(const ChunkSrc& src, uint32_t max_slots, uint32_t 
   out->max_key = max_key_for(U);
   alloc_result(out, s);
   CR_CUDA(cudaMemsetAsync(out->key_index, 0xFF, (size_t(out->max_key) + 1u) * 2u, s));
+  ProfileScope prof(CR_KERNEL_UPLOAD_EMIT, s);
   if (vec) k_emit<true><<<max_slots, kEmitThreads, 0, s>>>(src, max_slots, plan, d_hdr, *out);
   else k_emit<false><<<max_slots, kEmitThreads, 0, s>>>(src, max_slots, plan, d_hdr, *out);
   CR_CUDA(cudaGetLastError());
@@ -546,6 +547,7 @@ void upload_device_ids(const uint32_t* d_ids, uint64_t n, uint32_t U, uint32_t t
   const int vec = (reinterpret_cast<uintptr_t>(d_ids) & 15u) == 0;
   if (dense) {
     CR_CUDA(cudaMemsetAsync(base, 0, words_b + 64, s));
+    ProfileScope prof(CR_KERNEL_UPLOAD_SCATTER, s);
     k_scatter<<<grid_for(n, 8), 256, 0, s>>>(d_ids, n, U, nullptr, words, d_err, vec);
   } else {
     unsigned long long* presence = reinterpret_cast<unsigned long long*>(aux + 64);

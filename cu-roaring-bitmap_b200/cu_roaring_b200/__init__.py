@@ -35,7 +35,7 @@ EXPORTED_SYMBOLS = (
     "cr_promote_auto", "cr_deep_copy", "cr_set_operation", "cr_multi_and", "cr_multi_or",
     "cr_decompress_to_bitset", "cr_decompress_to_bitset_alloc", "cr_enumerate_ids_i64",
     "cr_enumerate_ids_u32", "cr_enumerate_ids_alloc", "cr_contains_batch", "cr_filtered_topk",
-    "cr_row_norms", "cr_topk_merge",
+    "cr_row_norms", "cr_topk_merge", "cr_profile_enable", "cr_profile_last_ms",
 )
 
 
@@ -82,6 +82,8 @@ _sigs = {
     "cr_filtered_topk": ([_vp, _vp, _u64, _u32, _vp, _u32, _P, _u64, _u32, _i32, _vp, _vp, _vp], _i32),
     "cr_row_norms": ([_vp, _u64, _u32, _vp, _vp], _i32),
     "cr_topk_merge": ([_vp, _vp, _u32, _u32, _u32, _i32, _vp, _vp, _vp], _i32),
+    "cr_profile_enable": ([_i32], _i32),
+    "cr_profile_last_ms": ([_i32, C.POINTER(C.c_float)], _i32),
 }
 for _name, (_args, _res) in _sigs.items():
     _f = getattr(_lib, _name)
@@ -374,3 +376,18 @@ def topk_merge(dist_parts, id_parts, k: int, metric: int = METRIC_IP, stream=Non
     _check(_lib.cr_topk_merge(_dev_ptr(dist_parts), _dev_ptr(id_parts), p, q, k, metric, _dev_ptr(out_d),
                               _dev_ptr(out_i), _stream_ptr(stream)), "topk_merge")
     return out_d, out_i
+
+
+# ------------------------------------------------------------- measurement
+
+KERNEL_TOPK, KERNEL_CONTAINS, KERNEL_SETOP, KERNEL_UPLOAD_SCATTER, KERNEL_UPLOAD_EMIT, KERNEL_DECOMPRESS = range(6)
+
+
+def profile_enable(on: bool = True) -> None:
+    _lib.cr_profile_enable(int(on))
+
+
+def profile_last_ms(kernel: int) -> float:
+    v = C.c_float()
+    _check(_lib.cr_profile_last_ms(kernel, C.byref(v)), "profile_last_ms")
+    return v.value

@@ -6,7 +6,12 @@
 // reads the container metadata, which it broadcasts with __shfl_sync. Every
 // lane then reads its own payload word / searches its own container.
 //
-// Must be called by all lanes in __activemask() (the usual convergent call).
+// Warp-synchronous: call it from converged code. In a kernel with a bounds
+// check, let every lane call it (out-of-range lanes on any valid ID, result
+// discarded) instead of calling it inside `if (i < n)`: __activemask() does
+// not guarantee that the lanes it reports execute the following *_sync
+// intrinsics together, and on sm_100 a mismatch raises an illegal
+// instruction.
 #pragma once
 #include "roaring_view.cuh"
 

@@ -31,7 +31,8 @@ __global__ void user_warp_contains(cu_roaring::GpuRoaringView v, const uint32_t*
                                    uint32_t n)
 {
   const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < n) out[i] = cu_roaring::warp_contains(v, q[i]);
+  const bool hit = cu_roaring::warp_contains(v, i < n ? q[i] : 0u);  // all lanes call it
+  if (i < n) out[i] = hit;
 }
 
 static std::vector<uint8_t> query(const cu_roaring::GpuRoaring& bm, const std::vector<uint32_t>& q,

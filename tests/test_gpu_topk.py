@@ -1,0 +1,115 @@
+"""GPU: the fused filtered top-k (tcgen05 GEMM + bitmap predicate + select)
+against the exact fp32 oracle.
+
+Tolerance: distances within 1e-3 relative; id sets
+equal except where the oracle's k-th distance ties within that tolerance.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+RTOL = 1e-3
+
+
+def make_data(n, q, dim=128, seed=0):
+    rng = np.random.default_rng(seed)
+    db = rng.standard_normal((n, dim)).astype(np.float32)
+    db /= np.linalg.norm(db, axis=1, keepdims=True)
+    qs = rng.standard_normal((q, dim)).astype(np.float32)
+    qs /= np.linalg.norm(qs, axis=1, keepdims=True)
+    return db.astype(np.float16), qs.astype(np.float16)
+
+
+def check_topk(d_gpu, i_gpu, d_ref, i_ref, metric):
+    k = d_ref.shape[1]
+    valid = i_ref >= 0
+    assert np.array_equal(valid, i_gpu >= 0), "number of results differs"
+    scale = np.maximum(np.abs(d_ref), 1e-3)
+    diff = np.abs(np.where(valid, d_gpu - d_ref, 0.0))
+    assert (diff <= RTOL * scale + 1e-6).all(), f"max distance error {diff.max()}"
+    for qi in range(d_ref.shape[0]):
+        a = set(i_gpu[qi][valid[qi]].tolist())
+        b = set(i_ref[qi][valid[qi]].tolist())
+        if a == b:
+            continue
+        kth = d_ref[qi][valid[qi]][-1]
+        # Only boundary ties may differ.
+        for r in a ^ b:
+            pos = np.flatnonzero(i_gpu[qi] == r)
+            dist = d_gpu[qi][pos[0]] if pos.size else d_ref[qi][np.flatnonzero(i_ref[qi] == r)[0]]
+            assert abs(dist - kth) <= RTOL * max(abs(kth), 1e-3) + 1e-6, f"query {qi}: id {r}"
+    _ = k
+
+
+@pytest.fixture(scope="module")
+def torch_():
+    import torch
+
+    return torch
+
+
+@pytest.mark.parametrize("n,q,k", [(5000, 37, 10), (20000, 300, 100), (70001, 129, 256), (1000, 5, 1)])
+@pytest.mark.parametrize("metric", [0, 1])
+@pytest.mark.parametrize("pass_rate", [None, 0.5, 0.01])
+def test_topk_matches_oracle(cr, oracle, torch_, n, q, k, metric, pass_rate):
+    db, qs = make_data(n, q, seed=n + q)
+    filt = None
+    pass_bits = None
+    if pass_rate is not None:
+        rng = np.random.default_rng(3)
+        ids = np.flatnonzero(rng.random(n) < pass_rate).astype(np.uint32)
+        filt = cr.upload_from_ids(ids, n)
+        words = np.zeros((n + 31) // 32, dtype=np.uint32)
+        np.bitwise_or.at(words, ids // 32, (1 << (ids % 32)).astype(np.uint32))
+        pass_bits = words
+    d_ref, i_ref = oracle.topk(db, qs, k, metric, pass_bits)
+    ddb = torch_.from_numpy(db).cuda()
+    dq = torch_.from_numpy(qs).cuda()
+    norms = cr.row_norms(ddb) if metric == 1 else None
+    d, i = cr.filtered_topk(ddb, dq, k, metric=metric, filter=filt, db_norms=norms)
+    check_topk(d.cpu().numpy(), i.cpu().numpy(), d_ref, i_ref, metric)
+    if filt is not None:
+        filt.free()
+
+
+def test_topk_row_offset_and_merge(cr, oracle, torch_):
+    """Sharded search: two row ranges with global IDs, then cr_topk_merge."""
+    n, q, k = 30000, 64, 50
+    db, qs = make_data(n, q, seed=9)
+    rng = np.random.default_rng(4)
+    ids = np.flatnonzero(rng.random(n) < 0.1).astype(np.uint32)
+    filt = cr.upload_from_ids(ids, n)
+    words = np.zeros((n + 31) // 32, dtype=np.uint32)
+    np.bitwise_or.at(words, ids // 32, (1 << (ids % 32)).astype(np.uint32))
+    for metric in (0, 1):
+        d_ref, i_ref = oracle.topk(db, qs, k, metric, words)
+        dq = torch_.from_numpy(qs).cuda()
+        parts_d, parts_i = [], []
+        for lo, hi in ((0, 12288), (12288, n)):
+            ddb = torch_.from_numpy(np.ascontiguousarray(db[lo:hi])).cuda()
+            d, i = cr.filtered_topk(ddb, dq, k, metric=metric, filter=filt, row_offset=lo)
+            parts_d.append(d)
+            parts_i.append(i)
+        d, i = cr.topk_merge(torch_.stack(parts_d), torch_.stack(parts_i), k, metric=metric)
+        check_topk(d.cpu().numpy(), i.cpu().numpy(), d_ref, i_ref, metric)
+    filt.free()
+
+
+def test_topk_against_torch_fp32_large(cr, torch_):
+    """1M x 128, 1000 queries, k=100, 10% pass: against torch fp32 matmul."""
+    n, q, k = 1_000_000, 1000, 100
+    g = torch_.Generator(device="cuda").manual_seed(5)
+    db = torch_.nn.functional.normalize(torch_.randn(n, 128, device="cuda", generator=g), dim=1).half()
+    qs = torch_.nn.functional.normalize(torch_.randn(q, 128, device="cuda", generator=g), dim=1).half()
+    keep = torch_.rand(n, device="cuda", generator=g) < 0.1
+    ids = torch_.nonzero(keep).flatten().to(torch_.int32)
+    filt = cr.upload_from_ids(ids, n)
+    d, i = cr.filtered_topk(db, qs, k, metric=0, filter=filt)
+    scores = qs.float() @ db.float().T
+    scores[:, ~keep] = -float("inf")
+    ref_d, ref_i = torch_.topk(scores, k, dim=1)
+    check_topk(d.cpu().numpy(), i.cpu().numpy(), ref_d.cpu().numpy(), ref_i.cpu().numpy(), 0)
+    filt.free()
