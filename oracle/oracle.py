@@ -63,6 +63,9 @@ def lib():
             "or_enumerate": ([_IP, v], u64),
             "or_validate": ([_IP], i32),
             "or_topk": ([v, u64, u32, v, u32, v, u32, i32, v, v, i32], None),
+            "or_topk_f32": ([v, v, u64, u32, v, u32, v, u32, i32, v, v, i32], None),
+            "or_widen_f16": ([v, u64, v], None),
+            "or_row_norms_f32": ([v, u64, u32, v], None),
         }
         for name, (a, r) in sig.items():
             f = getattr(_lib, name)
@@ -198,3 +201,26 @@ def topk(db_f16: np.ndarray, queries_f16: np.ndarray, k: int, metric: int = 0,
     lib().or_topk(db.ctypes.data, n, d, q.ctypes.data, nq, pb.ctypes.data if pb is not None else None,
                   k, metric, dist.ctypes.data, ids.ctypes.data, threads or os.cpu_count() or 1)
     return dist, ids
+
+
+class F32Database:
+    """A database widened to fp32 once, for repeated timed CPU top-k calls."""
+
+    def __init__(self, db_f16: np.ndarray):
+        h = np.ascontiguousarray(db_f16).view(np.uint16)
+        self.n, self.dim = h.shape
+        self.f = np.empty((self.n, self.dim), dtype=np.float32)
+        lib().or_widen_f16(h.ctypes.data, h.size, self.f.ctypes.data)
+        self.norms = np.empty(self.n, dtype=np.float32)
+        lib().or_row_norms_f32(self.f.ctypes.data, self.n, self.dim, self.norms.ctypes.data)
+
+    def topk(self, queries_f16, k, metric=0, pass_bits=None, threads=0):
+        q = np.ascontiguousarray(queries_f16).view(np.uint16)
+        nq = q.shape[0]
+        dist = np.zeros((nq, k), dtype=np.float32)
+        ids = np.zeros((nq, k), dtype=np.int64)
+        pb = None if pass_bits is None else np.ascontiguousarray(pass_bits, dtype=np.uint32)
+        lib().or_topk_f32(self.f.ctypes.data, self.norms.ctypes.data, self.n, self.dim, q.ctypes.data, nq,
+                          pb.ctypes.data if pb is not None else None, k, metric, dist.ctypes.data,
+                          ids.ctypes.data, threads or os.cpu_count() or 1)
+        return dist, ids

@@ -744,21 +744,38 @@ static void* topk_worker(void* p)
 /* Exact fp32 brute force: fp16 inputs widened, IP = sum q_d x_d, L2 =
  * |x|^2 - 2 q.x + |q|^2, the filter applied before selection, ties broken
  * by the smaller row id. */
+void or_widen_f16(const uint16_t* src, uint64_t n, float* dst)
+{
+  for (uint64_t i = 0; i < n; ++i) dst[i] = half_to_float(src[i]);
+}
+
+void or_row_norms_f32(const float* dbf, uint64_t n_rows, uint32_t dim, float* norms)
+{
+  for (uint64_t r = 0; r < n_rows; ++r) {
+    float s = 0.f;
+    for (uint32_t d = 0; d < dim; ++d) s += dbf[r * dim + d] * dbf[r * dim + d];
+    norms[r] = s;
+  }
+}
+
 void or_topk(const uint16_t* db, uint64_t n_rows, uint32_t dim, const uint16_t* queries,
              uint32_t n_queries, const uint32_t* pass_bits, uint32_t k, int metric,
              float* out_dist, int64_t* out_ids, int n_threads)
 {
   float* dbf = (float*)malloc(sizeof(float) * n_rows * dim);
   float* norms = (float*)malloc(sizeof(float) * (n_rows + 1));
-  for (uint64_t r = 0; r < n_rows; ++r) {
-    float s = 0.f;
-    for (uint32_t d = 0; d < dim; ++d) {
-      float v = half_to_float(db[r * dim + d]);
-      dbf[r * dim + d] = v;
-      s += v * v;
-    }
-    norms[r] = s;
-  }
+  or_widen_f16(db, n_rows * dim, dbf);
+  or_row_norms_f32(dbf, n_rows, dim, norms);
+  or_topk_f32(dbf, norms, n_rows, dim, queries, n_queries, pass_bits, k, metric, out_dist, out_ids,
+              n_threads);
+  free(dbf);
+  free(norms);
+}
+
+void or_topk_f32(const float* dbf, const float* norms, uint64_t n_rows, uint32_t dim,
+                 const uint16_t* queries, uint32_t n_queries, const uint32_t* pass_bits, uint32_t k,
+                 int metric, float* out_dist, int64_t* out_ids, int n_threads)
+{
   if (n_threads < 1) n_threads = 1;
   if (n_threads > 256) n_threads = 256;
   pthread_t th[256];
@@ -773,6 +790,4 @@ void or_topk(const uint16_t* db, uint64_t n_rows, uint32_t dim, const uint16_t* 
     pthread_create(&th[t], NULL, topk_worker, j);
   }
   for (int t = 0; t < n_threads; ++t) pthread_join(th[t], NULL);
-  free(dbf);
-  free(norms);
 }

@@ -82,6 +82,14 @@ void or_topk(const uint16_t* db, uint64_t n_rows, uint32_t dim, const uint16_t* 
              uint32_t n_queries, const uint32_t* pass_bits, uint32_t k, int metric,
              float* out_dist, int64_t* out_ids, int n_threads);
 
+/* Same with a pre-widened fp32 database and its squared norms (so a timed
+ * CPU baseline does not re-widen the database every call). */
+void or_topk_f32(const float* dbf, const float* norms, uint64_t n_rows, uint32_t dim,
+                 const uint16_t* queries, uint32_t n_queries, const uint32_t* pass_bits, uint32_t k,
+                 int metric, float* out_dist, int64_t* out_ids, int n_threads);
+void or_widen_f16(const uint16_t* src, uint64_t n, float* dst);
+void or_row_norms_f32(const float* dbf, uint64_t n_rows, uint32_t dim, float* norms);
+
 #ifdef __cplusplus
 }
 #endif
