@@ -15,8 +15,10 @@
 //           chunk the filter word (one u32 of the shard's pass bitset) is
 //           read first; chunks with no passing row are never loaded from
 //           TMEM; passing scores are compared with the thread's running k-th
-//           best and rare survivors go to a 32-entry shared-memory buffer,
-//           merged into a per-thread sorted top-k list when full.
+//           best and rare survivors go to a per-query shared-memory buffer;
+//           buffers holding >= 32 entries are merged by the whole warp
+//           (bitonic sort + chunked bitonic merge) into per-query sorted
+//           top-k lists kept in global memory (L2-resident, coalesced).
 //
 // A second kernel merges the per-slice lists of each query (bitonic sort in
 // shared memory) and converts internal scores to distances. Internal score
@@ -42,7 +44,7 @@ constexpr uint32_t BM = 128;       // queries per CTA (UMMA M, TMEM lanes)
 constexpr uint32_t BN = 256;       // database rows per tile (UMMA N)
 constexpr uint32_t DIM = 128;      // K
 constexpr uint32_t STAGES = 2;
-constexpr uint32_t BUF = 32;       // candidate buffer entries per query
+constexpr uint32_t BUF = 64;       // candidate buffer entries per query (flushed at >= 32)
 constexpr uint32_t THREADS = 192;  // 6 warps
 constexpr uint32_t KB_BYTES_Q = BM * 128;    // one 64-dim K-block of the query tile
 constexpr uint32_t KB_BYTES_DB = BN * 128;   // one 64-dim K-block of a database tile
@@ -61,7 +63,7 @@ struct TopkParams {
   uint32_t n_tiles, tiles_per_slice;
   const uint32_t* pass;  // local pass bitset, null = every row passes
   const float* norms;    // squared row norms (L2)
-  float* list_s;         // per-thread sorted lists: [cta][2][k][BM]
+  float* list_s;         // per-query sorted lists: [cta][BM][2][k]
   uint32_t* list_r;
   float* part_s;         // [slice][Q][k] internal scores
   int64_t* part_id;
@@ -74,43 +76,75 @@ __device__ __forceinline__ bool better(float as, uint32_t ar, float bs, uint32_t
   return as > bs || (as == bs && ar < br);
 }
 
-// Merges this thread's nb buffered candidates into its sorted list.
-__device__ void flush_buffer(float* bs, uint32_t* br, uint32_t nb, uint32_t t, float* Ls,
-                             uint32_t* Lr, uint32_t k, uint32_t& half, uint32_t& cnt,
-                             float& thr_s, uint32_t& thr_r)
+// One (score, row) pair held by each lane of a warp.
+struct Cand {
+  float s;
+  uint32_t r;
+};
+
+__device__ __forceinline__ Cand shfl_xor(Cand c, int m)
 {
-  for (uint32_t i = 1; i < nb; ++i) {  // insertion sort, best first
-    const float s = bs[i * BM + t];
-    const uint32_t r = br[i * BM + t];
-    uint32_t j = i;
-    while (j > 0 && better(s, r, bs[(j - 1) * BM + t], br[(j - 1) * BM + t])) {
-      bs[j * BM + t] = bs[(j - 1) * BM + t];
-      br[j * BM + t] = br[(j - 1) * BM + t];
-      --j;
-    }
-    bs[j * BM + t] = s;
-    br[j * BM + t] = r;
+  return {__shfl_xor_sync(0xFFFFFFFFu, c.s, m), __shfl_xor_sync(0xFFFFFFFFu, c.r, m)};
+}
+
+// Compare-exchange with the lane at distance `stride`: the lower lane keeps
+// the better element when `better_low`, else the worse one.
+__device__ __forceinline__ Cand cmpx(Cand v, int stride, bool better_low)
+{
+  const Cand o = shfl_xor(v, stride);
+  const bool low = (threadIdx.x & stride) == 0;
+  const bool v_better = better(v.s, v.r, o.s, o.r);
+  return (low == better_low) == v_better ? v : o;
+}
+
+// Warp bitonic sort of 32 candidates, best in lane 0.
+__device__ __forceinline__ Cand warp_sort(Cand v)
+{
+  const uint32_t lane = threadIdx.x & 31;
+#pragma unroll
+  for (int size = 2; size <= 32; size <<= 1)
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1)
+      v = cmpx(v, stride, (lane & size) == 0 || size == 32);
+  return v;
+}
+
+// Sorts a bitonic 32-sequence across the warp, best in lane 0.
+__device__ __forceinline__ Cand warp_bitonic_merge(Cand v)
+{
+#pragma unroll
+  for (int stride = 16; stride > 0; stride >>= 1) v = cmpx(v, stride, true);
+  return v;
+}
+
+// Merges up to 32 candidates (entries [e0, e1) of one lane's shared buffer)
+// into that lane's sorted list, all 32 lanes cooperating: the new entries are
+// warp-sorted, then the list is consumed in coalesced 32-entry chunks, each
+// bitonically merged with the carried 32 best-not-yet-output candidates.
+// Returns the list's new length; *kth gets its k-th entry when full.
+__device__ uint32_t warp_merge_into(const float* bs, const uint32_t* br, uint32_t e0, uint32_t e1,
+                                    const float* src_s, const uint32_t* src_r, float* dst_s,
+                                    uint32_t* dst_r, uint32_t cnt, uint32_t k, Cand* kth)
+{
+  const uint32_t lane = threadIdx.x & 31;
+  Cand b{-INFINITY, 0xFFFFFFFFu};
+  if (e0 + lane < e1) b = {bs[e0 + lane], br[e0 + lane]};
+  b = warp_sort(b);
+  const uint32_t total = min(k, cnt + (e1 - e0));
+  for (uint32_t c = 0; c * 32 < total; ++c) {
+    const uint32_t i = c * 32 + lane;
+    Cand a{-INFINITY, 0xFFFFFFFFu};
+    if (i < cnt) a = {src_s[i], src_r[i]};
+    // a is sorted best-first, b reversed -> one bitonic 64-sequence; split it.
+    Cand rb{__shfl_sync(0xFFFFFFFFu, b.s, 31 - lane), __shfl_sync(0xFFFFFFFFu, b.r, 31 - lane)};
+    const bool a_better = better(a.s, a.r, rb.s, rb.r);
+    Cand top = a_better ? a : rb, bot = a_better ? rb : a;
+    top = warp_bitonic_merge(top);
+    b = warp_bitonic_merge(bot);
+    if (i < total) { dst_s[i] = top.s; dst_r[i] = top.r; }
+    if (i == k - 1) *kth = top;
   }
-  const uint32_t src = half, dst = half ^ 1u;
-  uint32_t i = 0, j = 0, o = 0;
-  while (o < k && (i < cnt || j < nb)) {
-    const size_t si = (size_t(src) * k + i) * BM + t;
-    bool take_list;
-    if (i >= cnt) take_list = false;
-    else if (j >= nb) take_list = true;
-    else take_list = better(Ls[si], Lr[si], bs[j * BM + t], br[j * BM + t]);
-    const size_t so = (size_t(dst) * k + o) * BM + t;
-    if (take_list) { Ls[so] = Ls[si]; Lr[so] = Lr[si]; ++i; }
-    else { Ls[so] = bs[j * BM + t]; Lr[so] = br[j * BM + t]; ++j; }
-    ++o;
-  }
-  cnt = o;
-  half = dst;
-  if (cnt == k) {
-    const size_t sl = (size_t(dst) * k + k - 1) * BM + t;
-    thr_s = Ls[sl];
-    thr_r = Lr[sl];
-  }
+  return total;
 }
 
 __global__ void __launch_bounds__(THREADS, 1)
@@ -195,11 +229,49 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t qi = qt * BM + t_local;
     const bool valid_q = qi < p.n_queries;
     const size_t cta = size_t(slice) * gridDim.x + qt;
-    float* Ls = p.list_s + cta * 2 * p.k * BM;
-    uint32_t* Lr = p.list_r + cta * 2 * p.k * BM;
+    // This warp's 32 lists: [lane][half][k], contiguous per query.
+    float* Lw_s = p.list_s + (cta * BM + quarter * 32) * 2 * p.k;
+    uint32_t* Lw_r = p.list_r + (cta * BM + quarter * 32) * 2 * p.k;
+    float* mybuf_s = buf_s + t_local * BUF;
+    uint32_t* mybuf_r = buf_r + t_local * BUF;
     uint32_t half = 0, cnt = 0, nb = 0, thr_r = 0xFFFFFFFFu;
     float thr_s = -INFINITY;
     const bool l2 = p.metric == CR_METRIC_L2;
+
+    // Warp-cooperative merge of every lane whose buffer holds >= `min_fill`.
+    auto flush = [&](uint32_t min_fill) {
+      uint32_t need = __ballot_sync(0xFFFFFFFFu, nb >= min_fill && nb > 0);
+      while (need) {
+        const uint32_t f = __ffs(need) - 1;
+        need &= need - 1;
+        const uint32_t f_nb = __shfl_sync(0xFFFFFFFFu, nb, f);
+        uint32_t f_cnt = __shfl_sync(0xFFFFFFFFu, cnt, f);
+        uint32_t f_half = __shfl_sync(0xFFFFFFFFu, half, f);
+        const float* fb_s = buf_s + (quarter * 32 + f) * BUF;
+        const uint32_t* fb_r = buf_r + (quarter * 32 + f) * BUF;
+        float* fl_s = Lw_s + size_t(f) * 2 * p.k;
+        uint32_t* fl_r = Lw_r + size_t(f) * 2 * p.k;
+        Cand kth{-INFINITY, 0xFFFFFFFFu};
+        for (uint32_t e0 = 0; e0 < f_nb; e0 += 32) {
+          const uint32_t src = f_half, dst = f_half ^ 1u;
+          f_cnt = warp_merge_into(fb_s, fb_r, e0, min(f_nb, e0 + 32), fl_s + src * p.k, fl_r + src * p.k,
+                                  fl_s + dst * p.k, fl_r + dst * p.k, f_cnt, p.k, &kth);
+          f_half = dst;
+          __syncwarp();
+        }
+        // The lane that wrote entry k-1 (if any) broadcasts the new k-th best.
+        const uint32_t owner = (p.k - 1) & 31u;
+        kth.s = __shfl_sync(0xFFFFFFFFu, kth.s, owner);
+        kth.r = __shfl_sync(0xFFFFFFFFu, kth.r, owner);
+        if (lane == f) {
+          nb = 0;
+          cnt = f_cnt;
+          half = f_half;
+          if (cnt == p.k) { thr_s = kth.s; thr_r = kth.r; }
+        }
+      }
+    };
+
     for (uint32_t t = t0; t < t1; ++t) {
       const uint32_t it = t - t0, a = it & 1u;
       if (!mbar_wait(acc_full + a, (it >> 1) & 1u, p.err, 16u)) break;
@@ -215,33 +287,38 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (m == 0) continue;
         float v[32];
         tmem_ld32(tmem + ((quarter * 32u) << 16) + a * BN + c * 32, v);
-        if (!valid_q) continue;
+        if (valid_q) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          if (!((m >> j) & 1u)) continue;
-          const uint32_t r = r0 + j;
-          const float sc = l2 ? 2.f * v[j] - __ldg(p.norms + r) : v[j];
-          if (better(sc, r, thr_s, thr_r)) {
-            buf_s[nb * BM + t_local] = sc;
-            buf_r[nb * BM + t_local] = r;
-            if (++nb == BUF) {
-              flush_buffer(buf_s, buf_r, nb, t_local, Ls, Lr, p.k, half, cnt, thr_s, thr_r);
-              nb = 0;
+          for (int j = 0; j < 32; ++j) {
+            if (!((m >> j) & 1u)) continue;
+            const uint32_t r = r0 + j;
+            const float sc = l2 ? 2.f * v[j] - __ldg(p.norms + r) : v[j];
+            if (better(sc, r, thr_s, thr_r)) {
+              mybuf_s[nb] = sc;
+              mybuf_r[nb] = r;
+              ++nb;
             }
           }
         }
+        flush(32);  // at most 31 + 32 entries are ever buffered
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(acc_empty + a);
     }
-    if (valid_q) {
-      if (nb) flush_buffer(buf_s, buf_r, nb, t_local, Ls, Lr, p.k, half, cnt, thr_s, thr_r);
-      const size_t base = (size_t(slice) * p.n_queries + qi) * p.k;
-      for (uint32_t i = 0; i < p.k; ++i) {
-        const size_t si = (size_t(half) * p.k + i) * BM + t_local;
-        p.part_s[base + i] = i < cnt ? Ls[si] : -INFINITY;
-        p.part_id[base + i] = i < cnt ? int64_t(Lr[si]) + int64_t(p.row_offset) : int64_t(-1);
+    flush(1);
+    // Coalesced copy of each lane's final list into this slice's output.
+    for (uint32_t f = 0; f < 32; ++f) {
+      const uint32_t fq = qt * BM + quarter * 32 + f;
+      if (fq >= p.n_queries) break;
+      const uint32_t f_cnt = __shfl_sync(0xFFFFFFFFu, cnt, f);
+      const uint32_t f_half = __shfl_sync(0xFFFFFFFFu, half, f);
+      const float* ls = Lw_s + (size_t(f) * 2 + f_half) * p.k;
+      const uint32_t* lr = Lw_r + (size_t(f) * 2 + f_half) * p.k;
+      const size_t base = (size_t(slice) * p.n_queries + fq) * p.k;
+      for (uint32_t i = lane; i < p.k; i += 32) {
+        p.part_s[base + i] = i < f_cnt ? ls[i] : -INFINITY;
+        p.part_id[base + i] = i < f_cnt ? int64_t(lr[i]) + int64_t(p.row_offset) : int64_t(-1);
       }
     }
   }
