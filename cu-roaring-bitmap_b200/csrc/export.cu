@@ -9,6 +9,8 @@
 // negated bitmaps enumerate the complement (the reference ignores
 // `negated`, src/to_csr.cu:36-131).
 #include <algorithm>
+#include <mutex>
+#include <string>
 
 #include "chunk_ops.cuh"
 #include "cu_roaring/device/make_view.cuh"
@@ -347,5 +349,105 @@ extern "C" int cr_promote_auto(const cr_gpu_roaring* bm, cr_stream_t stream, int
   const uint32_t t = resolve_auto(bm->universe_size, device_id);
   if (t == 0 && (bm->n_array_containers || bm->n_run_containers)) promote_to_bitmap(bm, out, s);
   else deep_copy(bm, out, s);
+  CR_API_END
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free enumerate_ids (no counterpart in the reference).
+//
+// For callers that may not allocate device memory while they run: engines
+// that hand all of a GPU's memory to their own pool at start-up, or
+// latency-critical paths where a cudaMallocAsync (and the pool growth or
+// synchronisation it can cause) is not allowed. The scratch that
+// cr_enumerate_ids_u32 takes from the stream-ordered allocator (per-unit
+// counts, the tile scan, the output prefix, and a key index for bitmaps that
+// lack one) lives instead in one file-scope device array of
+// kNoAllocScratchBytes, which every GPU that loads this library holds until
+// the process exits.
+// ---------------------------------------------------------------------------
+
+namespace {
+constexpr uint32_t kNoAllocMaxUnits = 65536;  // containers or chunks: every valid bitmap
+constexpr size_t kNoAllocPrefixOff = 0;                                   // u64[65536]
+constexpr size_t kNoAllocTilesOff = kNoAllocPrefixOff + kNoAllocMaxUnits * 8;  // u64[64]
+constexpr size_t kNoAllocCountsOff = kNoAllocTilesOff + 64 * 8;           // u32[65536]
+constexpr size_t kNoAllocKidxOff = kNoAllocCountsOff + kNoAllocMaxUnits * 4;   // u16[65536]
+constexpr size_t kNoAllocScratchBytes = kNoAllocKidxOff + kNoAllocMaxUnits * 2;
+}  // namespace
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of g_noalloc_scratch on the current device. The first call
+// on each device resolves it with cudaGetSymbolAddress (with that device
+// current); later calls reuse the cached address.
+static unsigned char* noalloc_scratch()
+{
+  static std::mutex mu;
+  static unsigned char* addr[64] = {};
+  int dev = 0;
+  CR_CUDA(cudaGetDevice(&dev));
+  CR_REQUIRE(dev >= 0 && dev < 64, "cr_enumerate_ids_u32_noalloc: device ordinal out of range");
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      cudaGetLastError();
+      fail(CR_ERR_CUDA, std::string("cr_enumerate_ids_u32_noalloc: cudaGetSymbolAddress failed: ") +
+                            cudaGetErrorString(e));
+    }
+    addr[dev] = static_cast<unsigned char*>(p);
+  }
+  return addr[dev];
+}
+
+extern "C" int cr_enumerate_ids_u32_noalloc(const cr_gpu_roaring* bm, uint32_t* d_output,
+                                            cr_stream_t stream)
+{
+  CR_API_BEGIN
+  CR_REQUIRE(bm != nullptr, "cr_enumerate_ids_u32_noalloc: null bitmap");
+  if (bm->total_cardinality == 0) return CR_OK;
+  CR_REQUIRE(d_output != nullptr, "cr_enumerate_ids_u32_noalloc: null output");
+  const uint32_t n_units = bm->negated ? n_chunks_for(bm->universe_size) : bm->n_containers;
+  if (n_units == 0) return CR_OK;
+  if (n_units > kNoAllocMaxUnits)
+    fail(CR_ERR_INVALID, "cr_enumerate_ids_u32_noalloc: " + std::to_string(n_units) +
+                             " containers exceed the fixed scratch limit of 65536");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  unsigned char* scratch = noalloc_scratch();
+  unsigned long long* prefix = reinterpret_cast<unsigned long long*>(scratch + kNoAllocPrefixOff);
+  unsigned long long* tiles = reinterpret_cast<unsigned long long*>(scratch + kNoAllocTilesOff);
+  uint32_t* counts = reinterpret_cast<uint32_t*>(scratch + kNoAllocCountsOff);
+  DevBitmap b{};
+  b.keys = bm->keys;
+  b.types = bm->types;
+  b.offsets = bm->offsets;
+  b.cards = bm->cardinalities;
+  b.bitmap = bm->bitmap_data;
+  b.array = bm->array_data;
+  b.run = bm->run_data;
+  b.n = bm->n_containers;
+  b.universe = bm->universe_size;
+  b.negated = bm->negated ? 1u : 0u;
+  b.key_index = bm->key_index;
+  b.max_key = bm->max_key;
+  if (bm->n_containers == 0) {
+    b.key_index = nullptr;
+    b.max_key = 0;
+  } else if (bm->key_index == nullptr) {
+    // No index on the input: build a full one in the static scratch.
+    uint16_t* kidx = reinterpret_cast<uint16_t*>(scratch + kNoAllocKidxOff);
+    build_key_index(bm->keys, bm->n_containers, kidx, kNoAllocMaxUnits, s);
+    b.key_index = kidx;
+    b.max_key = kNoAllocMaxUnits - 1;
+  }
+  // counts, tile sums and prefixes are fully rewritten below, so the
+  // previous call's contents never leak into this one.
+  const uint32_t n_tiles = div_up(n_units, kScanTile);
+  k_enum_count<<<div_up(n_units, 256), 256, 0, s>>>(b, n_units, counts);
+  k_scan_tiles<<<n_tiles, kScanTile, 0, s>>>(counts, n_units, tiles);
+  k_scan_apply<<<n_tiles, kScanTile, 0, s>>>(counts, n_units, tiles, prefix);
+  k_enum_emit<uint32_t><<<n_units, 256, 0, s>>>(b, prefix, d_output);
+  CR_CUDA(cudaGetLastError());
   CR_API_END
 }

@@ -34,7 +34,7 @@ EXPORTED_SYMBOLS = (
     "cr_gpu_roaring_free_async", "cr_resolve_auto_threshold", "cr_promote_to_bitmap",
     "cr_promote_auto", "cr_deep_copy", "cr_set_operation", "cr_multi_and", "cr_multi_or",
     "cr_decompress_to_bitset", "cr_decompress_to_bitset_alloc", "cr_enumerate_ids_i64",
-    "cr_enumerate_ids_u32", "cr_enumerate_ids_alloc", "cr_contains_batch", "cr_filtered_topk",
+    "cr_enumerate_ids_u32", "cr_enumerate_ids_alloc", "cr_enumerate_ids_u32_noalloc", "cr_contains_batch", "cr_filtered_topk",
     "cr_row_norms", "cr_topk_merge", "cr_profile_enable", "cr_profile_last_ms",
 )
 
@@ -78,6 +78,7 @@ _sigs = {
     "cr_enumerate_ids_i64": ([_P, _vp, _vp], _i32),
     "cr_enumerate_ids_u32": ([_P, _vp, _vp], _i32),
     "cr_enumerate_ids_alloc": ([_P, _vp, C.POINTER(_vp)], _i32),
+    "cr_enumerate_ids_u32_noalloc": ([_P, _vp, _vp], _i32),
     "cr_contains_batch": ([_P, _vp, _u64, _vp, _i32, _vp], _i32),
     "cr_filtered_topk": ([_vp, _vp, _u64, _u32, _vp, _u32, _P, _u64, _u32, _i32, _vp, _vp, _vp], _i32),
     "cr_row_norms": ([_vp, _u64, _u32, _vp, _vp], _i32),

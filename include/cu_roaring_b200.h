@@ -152,6 +152,18 @@ int cr_enumerate_ids_i64(const cr_gpu_roaring* bm, int64_t* d_output, cr_stream_
 int cr_enumerate_ids_u32(const cr_gpu_roaring* bm, uint32_t* d_output, cr_stream_t stream);
 int cr_enumerate_ids_alloc(const cr_gpu_roaring* bm, cr_stream_t stream, int64_t** d_out);
 
+/* Allocation-free form of cr_enumerate_ids_u32 (no counterpart in the
+ * reference). For callers that must not allocate device memory while they
+ * run, e.g. a server that gave all GPU memory to its own pool at start-up or
+ * a latency-critical path that forbids allocator calls. Its scratch is one
+ * fixed array of about 0.9 MiB inside the library, resident on every GPU that
+ * loads it; it covers any valid bitmap (at most 65536 containers/chunks) and
+ * larger inputs are rejected with CR_ERR_INVALID. The first call on a device
+ * looks up that array's device address; make that first call before any
+ * stream capture. All calls share the array, so calls that overlap on the GPU
+ * (different streams, or different host threads) race: serialise them. */
+int cr_enumerate_ids_u32_noalloc(const cr_gpu_roaring* bm, uint32_t* d_output, cr_stream_t stream);
+
 /* ---- Bulk point queries ------------------------------------------------------ */
 
 /* Bulk form of GpuRoaringView::contains / warp_contains (reference
