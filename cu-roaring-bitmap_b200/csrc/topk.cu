@@ -69,7 +69,21 @@ struct TopkParams {
   int64_t* part_id;
   uint64_t row_offset;
   uint32_t* err;
+  uint32_t* shared_thr;  // [Q] order-preserving bits of the best known k-th score
 };
+
+// Order-preserving map float -> uint32 (larger float -> larger key); 0 is
+// below every real score and decodes to -inf.
+__device__ __forceinline__ uint32_t score_key(float f)
+{
+  const uint32_t i = __float_as_uint(f);
+  return (i & 0x80000000u) ? ~i : (i | 0x80000000u);
+}
+__device__ __forceinline__ float key_score(uint32_t k)
+{
+  if (k == 0) return -INFINITY;
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
+}
 
 __device__ __forceinline__ bool better(float as, uint32_t ar, float bs, uint32_t br)
 {
@@ -267,16 +281,23 @@ __global__ void __launch_bounds__(THREADS, 1)
           nb = 0;
           cnt = f_cnt;
           half = f_half;
-          if (cnt == p.k) { thr_s = kth.s; thr_r = kth.r; }
+          if (cnt == p.k) {
+            thr_s = kth.s;
+            thr_r = kth.r;
+            atomicMax(p.shared_thr + qi, score_key(thr_s));
+          }
         }
       }
     };
 
+    float gthr = -INFINITY;  // bound shared by every slice of this query
     for (uint32_t t = t0; t < t1; ++t) {
       const uint32_t it = t - t0, a = it & 1u;
+      if (valid_q) gthr = fmaxf(gthr, key_score(__ldcg(p.shared_thr + qi)));
       if (!mbar_wait(acc_full + a, (it >> 1) & 1u, p.err, 16u)) break;
       tc_fence_after();
       const uint32_t row0 = t * BN;
+      const float bound = fmaxf(gthr, thr_s);
 #pragma unroll 1
       for (uint32_t c = 0; c < BN / 32; ++c) {
         const uint32_t r0 = row0 + c * 32;
@@ -287,14 +308,20 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (m == 0) continue;
         float v[32];
         tmem_ld32(tmem + ((quarter * 32u) << 16) + a * BN + c * 32, v);
-        if (valid_q) {
+        if (l2) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = 2.f * v[j] - __ldg(p.norms + r0 + j);
+        }
+        // Fast path: the best passing score of the chunk against the bound.
+        float mx = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) mx = fmaxf(mx, ((m >> j) & 1u) ? v[j] : -INFINITY);
+        if (valid_q && mx >= bound) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
-            if (!((m >> j) & 1u)) continue;
             const uint32_t r = r0 + j;
-            const float sc = l2 ? 2.f * v[j] - __ldg(p.norms + r) : v[j];
-            if (better(sc, r, thr_s, thr_r)) {
-              mybuf_s[nb] = sc;
+            if (((m >> j) & 1u) && v[j] >= gthr && better(v[j], r, thr_s, thr_r)) {
+              mybuf_s[nb] = v[j];
               mybuf_r[nb] = r;
               ++nb;
             }
@@ -563,7 +590,7 @@ extern "C" int cr_filtered_topk(const uint16_t* d_db, const float* d_db_norms, u
   const size_t list_b = ctas * 2 * k * BM * 4;
   const size_t part_b = size_t(slices) * n_queries * k;
   Scratch scr(list_b * 2 + part_b * 12 + (filter ? pass_words * 4 : 0) +
-                  ((l2 && !d_db_norms) ? n_rows * 4 : 0) + 64 + 256,
+                  ((l2 && !d_db_norms) ? n_rows * 4 : 0) + size_t(n_queries) * 4 + 64 + 256,
               s);
   char* p = scr.as<char>();
   TopkParams tp{};
@@ -601,7 +628,8 @@ extern "C" int cr_filtered_topk(const uint16_t* d_db, const float* d_db_norms, u
   }
   p = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(p) + 15) & ~uintptr_t(15));
   tp.err = reinterpret_cast<uint32_t*>(p);
-  CR_CUDA(cudaMemsetAsync(tp.err, 0, 4, s));
+  tp.shared_thr = tp.err + 4;
+  CR_CUDA(cudaMemsetAsync(tp.err, 0, 16 + size_t(n_queries) * 4, s));
   const CUtensorMap tq = make_map(d_queries, n_queries, BM);
   const CUtensorMap tdb = make_map(d_db, n_rows, BN);
   {
