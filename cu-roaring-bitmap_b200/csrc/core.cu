@@ -21,10 +21,32 @@ void check_cuda(cudaError_t e, const char* what, const char* file, int line)
                ":" + std::to_string(line));
 }
 
+// The stream-ordered allocator's default pool hands memory back to the driver
+// at every synchronisation (release threshold 0), which makes each call that
+// takes scratch re-map it. Keep freed memory cached in this process's pool
+// instead (once per device; the setting belongs to the process, not the GPU).
+static void keep_pool_memory()
+{
+  static std::mutex mu;
+  static bool done[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) { cudaGetLastError(); return; }
+  std::lock_guard<std::mutex> lock(mu);
+  if (done[dev]) return;
+  done[dev] = true;
+  cudaMemPool_t pool;
+  if (cudaDeviceGetDefaultMemPool(&pool, dev) == cudaSuccess) {
+    uint64_t keep = ~0ull;
+    cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+  }
+  cudaGetLastError();
+}
+
 void* dev_alloc(size_t bytes, cudaStream_t s)
 {
   void* p = nullptr;
   if (bytes == 0) return nullptr;
+  keep_pool_memory();
   const cudaError_t e = cudaMallocAsync(&p, bytes, s);
   if (e != cudaSuccess) {
     cudaGetLastError();

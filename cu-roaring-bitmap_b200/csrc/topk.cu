@@ -28,6 +28,8 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <cstdio>
+#include <cstdlib>
 #include <mutex>
 
 #include "chunk_ops.cuh"
@@ -44,17 +46,21 @@ constexpr uint32_t BM = 128;       // queries per CTA (UMMA M, TMEM lanes)
 constexpr uint32_t BN = 256;       // database rows per tile (UMMA N)
 constexpr uint32_t DIM = 128;      // K
 constexpr uint32_t STAGES = 2;
-constexpr uint32_t BUF = 64;       // candidate buffer entries per query (flushed at >= 32)
-constexpr uint32_t THREADS = 192;  // 6 warps
+constexpr uint32_t EPI_WARPS = 8;  // two per TMEM lane quarter, each on half the columns
+constexpr uint32_t EPI = EPI_WARPS * 32;
+constexpr uint32_t BUF = 64;       // candidate buffer entries per (query, half); flushed at >= 32
+constexpr uint32_t THREADS = 96 + EPI;  // producer, MMA, bound keeper, 8 epilogue warps
+constexpr uint32_t EPI_WARP0 = 3;        // first epilogue warp
 constexpr uint32_t KB_BYTES_Q = BM * 128;    // one 64-dim K-block of the query tile
 constexpr uint32_t KB_BYTES_DB = BN * 128;   // one 64-dim K-block of a database tile
 constexpr uint32_t STAGE_BYTES = 2 * KB_BYTES_DB;
 constexpr uint32_t SMEM_Q = 0;
 constexpr uint32_t SMEM_DB = SMEM_Q + 2 * KB_BYTES_Q;
 constexpr uint32_t SMEM_BUF_S = SMEM_DB + STAGES * STAGE_BYTES;
-constexpr uint32_t SMEM_BUF_R = SMEM_BUF_S + BUF * BM * 4;
-constexpr uint32_t SMEM_BAR = SMEM_BUF_R + BUF * BM * 4;
-constexpr uint32_t SMEM_TOTAL = SMEM_BAR + 128 + 1024;  // + alignment slack
+constexpr uint32_t SMEM_BUF_R = SMEM_BUF_S;
+constexpr uint32_t SMEM_BAR = SMEM_BUF_R;
+constexpr uint32_t SMEM_BOUND = SMEM_BAR + 128;          // float[BM] + done counter
+constexpr uint32_t SMEM_TOTAL = SMEM_BOUND + BM * 4 + 16 + 1024;  // + alignment slack
 constexpr uint32_t TMEM_COLS = 512;                     // two 256-column accumulators
 constexpr uint32_t kIdesc = idesc_f16_f32(BM, BN);
 
@@ -70,6 +76,12 @@ struct TopkParams {
   uint64_t row_offset;
   uint32_t* err;
   uint32_t* shared_thr;  // [Q] order-preserving bits of the best known k-th score
+  uint32_t debug;        // measurement only: 1 = skip the epilogue's score work
+  float* buf_s;          // per-CTA candidate buffers: [cta][EPI][BUF] (global, L2-resident)
+  uint32_t* buf_r;
+  uint32_t* pub;         // [Q][n_lists] published j-th best of every partial list (score keys)
+  uint32_t n_lists;      // partial lists per query (2 per slice)
+  uint32_t jth;          // ceil(k / n_lists)
 };
 
 // Order-preserving map float -> uint32 (larger float -> larger key); 0 is
@@ -138,25 +150,37 @@ __device__ __forceinline__ Cand warp_bitonic_merge(Cand v)
 // Returns the list's new length; *kth gets its k-th entry when full.
 __device__ uint32_t warp_merge_into(const float* bs, const uint32_t* br, uint32_t e0, uint32_t e1,
                                     const float* src_s, const uint32_t* src_r, float* dst_s,
-                                    uint32_t* dst_r, uint32_t cnt, uint32_t k, Cand* kth)
+                                    uint32_t* dst_r, uint32_t cnt, uint32_t k, Cand* kth,
+                                    uint32_t j, Cand* jth)
 {
   const uint32_t lane = threadIdx.x & 31;
-  Cand b{-INFINITY, 0xFFFFFFFFu};
-  if (e0 + lane < e1) b = {bs[e0 + lane], br[e0 + lane]};
-  b = warp_sort(b);
   const uint32_t total = min(k, cnt + (e1 - e0));
-  for (uint32_t c = 0; c * 32 < total; ++c) {
+  const uint32_t nch = (total + 31) / 32;  // <= 8 for k <= 256
+  // Issue every load first (list chunks and new entries are independent),
+  // so the merge pays about one L2 round trip.
+  Cand a[8];
+#pragma unroll
+  for (uint32_t c = 0; c < 8; ++c) {
+    a[c] = {-INFINITY, 0xFFFFFFFFu};
     const uint32_t i = c * 32 + lane;
-    Cand a{-INFINITY, 0xFFFFFFFFu};
-    if (i < cnt) a = {src_s[i], src_r[i]};
-    // a is sorted best-first, b reversed -> one bitonic 64-sequence; split it.
+    if (c < nch && i < cnt) a[c] = {__ldcg(src_s + i), __ldcg(src_r + i)};
+  }
+  Cand b{-INFINITY, 0xFFFFFFFFu};
+  if (e0 + lane < e1) b = {__ldcg(bs + e0 + lane), __ldcg(br + e0 + lane)};
+  b = warp_sort(b);
+#pragma unroll
+  for (uint32_t c = 0; c < 8; ++c) {
+    if (c >= nch) break;
+    const uint32_t i = c * 32 + lane;
+    // a[c] is sorted best-first, b reversed -> one bitonic 64-sequence; split it.
     Cand rb{__shfl_sync(0xFFFFFFFFu, b.s, 31 - lane), __shfl_sync(0xFFFFFFFFu, b.r, 31 - lane)};
-    const bool a_better = better(a.s, a.r, rb.s, rb.r);
-    Cand top = a_better ? a : rb, bot = a_better ? rb : a;
+    const bool a_better = better(a[c].s, a[c].r, rb.s, rb.r);
+    Cand top = a_better ? a[c] : rb, bot = a_better ? rb : a[c];
     top = warp_bitonic_merge(top);
     b = warp_bitonic_merge(bot);
     if (i < total) { dst_s[i] = top.s; dst_r[i] = top.r; }
     if (i == k - 1) *kth = top;
+    if (i == j - 1) *jth = top;
   }
   return total;
 }
@@ -170,8 +194,9 @@ __global__ void __launch_bounds__(THREADS, 1)
                                              ~uintptr_t(1023));
   uint8_t* sQ = smem + SMEM_Q;
   uint8_t* sDB = smem + SMEM_DB;
-  float* buf_s = reinterpret_cast<float*>(smem + SMEM_BUF_S);
-  uint32_t* buf_r = reinterpret_cast<uint32_t*>(smem + SMEM_BUF_R);
+  const size_t cta_id = size_t(blockIdx.y) * gridDim.x + blockIdx.x;
+  float* buf_s = p.buf_s + cta_id * EPI * BUF;
+  uint32_t* buf_r = p.buf_r + cta_id * EPI * BUF;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SMEM_BAR);
   uint64_t* q_full = bars + 0;
   uint64_t* full = bars + 1;       // [STAGES]
@@ -179,6 +204,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* acc_full = bars + 5;   // [2]
   uint64_t* acc_empty = bars + 7;  // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
+  float* s_bound = reinterpret_cast<float*>(smem + SMEM_BOUND);
+  uint32_t* s_done = reinterpret_cast<uint32_t*>(smem + SMEM_BOUND + BM * 4);
 
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t qt = blockIdx.x, slice = blockIdx.y;
@@ -188,9 +215,11 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (uint32_t s = 0; s < STAGES; ++s) { mbar_init(full + s, 1); mbar_init(empty + s, 1); }
-    for (uint32_t a = 0; a < 2; ++a) { mbar_init(acc_full + a, 1); mbar_init(acc_empty + a, 4); }
+    for (uint32_t a = 0; a < 2; ++a) { mbar_init(acc_full + a, 1); mbar_init(acc_empty + a, EPI_WARPS); }
     fence_mbar_init();
+    *s_done = 0;
   }
+  for (uint32_t i = threadIdx.x; i < BM; i += THREADS) s_bound[i] = -INFINITY;
   if (warp == 0) tmem_alloc(tmem_slot, TMEM_COLS);
   tc_fence_before();
   __syncthreads();
@@ -236,40 +265,70 @@ __global__ void __launch_bounds__(THREADS, 1)
         umma_commit(acc_full + a);
       }
     }
+  } else if (warp == 2) {
+    // ---------------- bound keeper: for each query of the tile, the minimum
+    // over all partial lists of their published jth best (a lower bound of
+    // the k-th best, see the epilogue), kept fresh in shared memory.
+    for (uint32_t iter = 0; iter < kSpinLimit; ++iter) {
+      for (uint32_t qq = lane; qq < BM; qq += 32) {
+        const uint32_t q2 = qt * BM + qq;
+        if (q2 >= p.n_queries) continue;
+        uint32_t m0 = 0xFFFFFFFFu, m1 = 0xFFFFFFFFu, m2 = 0xFFFFFFFFu, m3 = 0xFFFFFFFFu;
+        uint32_t l = 0;
+        for (; l + 4 <= p.n_lists; l += 4) {
+          m0 = min(m0, __ldcg(p.pub + size_t(l) * p.n_queries + q2));
+          m1 = min(m1, __ldcg(p.pub + size_t(l + 1) * p.n_queries + q2));
+          m2 = min(m2, __ldcg(p.pub + size_t(l + 2) * p.n_queries + q2));
+          m3 = min(m3, __ldcg(p.pub + size_t(l + 3) * p.n_queries + q2));
+        }
+        for (; l < p.n_lists; ++l) m0 = min(m0, __ldcg(p.pub + size_t(l) * p.n_queries + q2));
+        s_bound[qq] = key_score(min(min(m0, m1), min(m2, m3)));
+      }
+      if (*reinterpret_cast<volatile uint32_t*>(s_done) >= EPI_WARPS) break;
+      for (int z = 0; z < 20; ++z) __nanosleep(1000);  // the bound moves slowly: refresh every ~20 us
+    }
   } else {
-    // ---------------- epilogue: warps 2..5, one thread per query
+    // ---------------- epilogue: warps 3..10, one thread per (query, half)
     const uint32_t quarter = warp & 3u;               // TMEM lane quarter this warp may access
+    const uint32_t chalf = (warp - EPI_WARP0) >> 2;   // which 128 columns (rows of the tile)
     const uint32_t t_local = quarter * 32 + lane;     // query row inside the tile
+    const uint32_t e_local = chalf * BM + t_local;    // this thread's (half, query) slot
     const uint32_t qi = qt * BM + t_local;
     const bool valid_q = qi < p.n_queries;
     const size_t cta = size_t(slice) * gridDim.x + qt;
     // This warp's 32 lists: [lane][half][k], contiguous per query.
-    float* Lw_s = p.list_s + (cta * BM + quarter * 32) * 2 * p.k;
-    uint32_t* Lw_r = p.list_r + (cta * BM + quarter * 32) * 2 * p.k;
-    float* mybuf_s = buf_s + t_local * BUF;
-    uint32_t* mybuf_r = buf_r + t_local * BUF;
+    float* Lw_s = p.list_s + ((cta * 2 + chalf) * BM + quarter * 32) * 2 * p.k;
+    uint32_t* Lw_r = p.list_r + ((cta * 2 + chalf) * BM + quarter * 32) * 2 * p.k;
+    float* mybuf_s = buf_s + e_local * BUF;
+    uint32_t* mybuf_r = buf_r + e_local * BUF;
     uint32_t half = 0, cnt = 0, nb = 0, thr_r = 0xFFFFFFFFu;
     float thr_s = -INFINITY;
     const bool l2 = p.metric == CR_METRIC_L2;
 
     // Warp-cooperative merge of every lane whose buffer holds >= `min_fill`.
     auto flush = [&](uint32_t min_fill) {
+      __syncwarp();  // buffer appends (global stores) visible to the whole warp
       uint32_t need = __ballot_sync(0xFFFFFFFFu, nb >= min_fill && nb > 0);
+      if (p.debug == 4) { if (nb >= min_fill) nb = 0; need = 0; }
+      if (p.debug == 3 && lane == 0 && need) {
+        atomicAdd(p.err + 1, __popc(need));
+        atomicAdd(p.err + 2, 1u);
+      }
       while (need) {
         const uint32_t f = __ffs(need) - 1;
         need &= need - 1;
         const uint32_t f_nb = __shfl_sync(0xFFFFFFFFu, nb, f);
         uint32_t f_cnt = __shfl_sync(0xFFFFFFFFu, cnt, f);
         uint32_t f_half = __shfl_sync(0xFFFFFFFFu, half, f);
-        const float* fb_s = buf_s + (quarter * 32 + f) * BUF;
-        const uint32_t* fb_r = buf_r + (quarter * 32 + f) * BUF;
+        const float* fb_s = buf_s + (chalf * BM + quarter * 32 + f) * BUF;
+        const uint32_t* fb_r = buf_r + (chalf * BM + quarter * 32 + f) * BUF;
         float* fl_s = Lw_s + size_t(f) * 2 * p.k;
         uint32_t* fl_r = Lw_r + size_t(f) * 2 * p.k;
-        Cand kth{-INFINITY, 0xFFFFFFFFu};
+        Cand kth{-INFINITY, 0xFFFFFFFFu}, jth{-INFINITY, 0xFFFFFFFFu};
         for (uint32_t e0 = 0; e0 < f_nb; e0 += 32) {
           const uint32_t src = f_half, dst = f_half ^ 1u;
           f_cnt = warp_merge_into(fb_s, fb_r, e0, min(f_nb, e0 + 32), fl_s + src * p.k, fl_r + src * p.k,
-                                  fl_s + dst * p.k, fl_r + dst * p.k, f_cnt, p.k, &kth);
+                                  fl_s + dst * p.k, fl_r + dst * p.k, f_cnt, p.k, &kth, p.jth, &jth);
           f_half = dst;
           __syncwarp();
         }
@@ -277,7 +336,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         const uint32_t owner = (p.k - 1) & 31u;
         kth.s = __shfl_sync(0xFFFFFFFFu, kth.s, owner);
         kth.r = __shfl_sync(0xFFFFFFFFu, kth.r, owner);
+        jth.s = __shfl_sync(0xFFFFFFFFu, jth.s, (p.jth - 1) & 31u);
         if (lane == f) {
+          if (!(p.jth <= 3) && f_cnt >= p.jth)
+            p.pub[size_t(slice * 2 + chalf) * p.n_queries + qi] = score_key(jth.s);
           nb = 0;
           cnt = f_cnt;
           half = f_half;
@@ -291,15 +353,25 @@ __global__ void __launch_bounds__(THREADS, 1)
     };
 
     float gthr = -INFINITY;  // bound shared by every slice of this query
+    // Best three scores this list has taken in (list + buffer), to publish its
+    // jth best every tile when jth <= 3 without waiting for a merge.
+    float top1 = -INFINITY, top2 = -INFINITY, top3 = -INFINITY;
+    uint32_t published = 0;
+    const bool fast_pub = p.jth <= 3;
     for (uint32_t t = t0; t < t1; ++t) {
       const uint32_t it = t - t0, a = it & 1u;
-      if (valid_q) gthr = fmaxf(gthr, key_score(__ldcg(p.shared_thr + qi)));
+      if (valid_q) {
+        gthr = fmaxf(gthr, key_score(__ldcg(p.shared_thr + qi)));
+        // Every list holds >= jth entries >= its published jth best, and
+        // n_lists * jth >= k: the minimum over lists bounds the k-th best.
+        gthr = fmaxf(gthr, reinterpret_cast<volatile float*>(s_bound)[t_local]);
+      }
       if (!mbar_wait(acc_full + a, (it >> 1) & 1u, p.err, 16u)) break;
       tc_fence_after();
       const uint32_t row0 = t * BN;
       const float bound = fmaxf(gthr, thr_s);
 #pragma unroll 1
-      for (uint32_t c = 0; c < BN / 32; ++c) {
+      for (uint32_t c = chalf * 4; c < (p.debug == 1 ? 0u : chalf * 4 + 4); ++c) {
         const uint32_t r0 = row0 + c * 32;
         if (r0 >= p.n_rows) break;
         uint32_t m = p.pass ? __ldg(p.pass + (r0 >> 5)) : 0xFFFFFFFFu;
@@ -316,11 +388,26 @@ __global__ void __launch_bounds__(THREADS, 1)
         float mx = -INFINITY;
 #pragma unroll
         for (int j = 0; j < 32; ++j) mx = fmaxf(mx, ((m >> j) & 1u) ? v[j] : -INFINITY);
-        if (valid_q && mx >= bound) {
+        if (__any_sync(0xFFFFFFFFu, valid_q && mx >= bound) && p.debug != 2) {
+          // Candidate rows of this lane, then the union over the warp, so the
+          // rows nobody keeps cost one uniform branch each.
+          uint32_t cm = 0;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) cm |= (v[j] >= bound ? 1u : 0u) << j;
+          cm &= valid_q ? m : 0u;
+          const uint32_t any = __reduce_or_sync(0xFFFFFFFFu, cm);
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
+            if (!((any >> j) & 1u)) continue;
             const uint32_t r = r0 + j;
-            if (((m >> j) & 1u) && v[j] >= gthr && better(v[j], r, thr_s, thr_r)) {
+            if (((cm >> j) & 1u) && v[j] >= gthr && better(v[j], r, thr_s, thr_r)) {
+              if (p.debug == 3) atomicAdd(p.err + 3, 1u);
+              if (fast_pub) {
+                const float x = v[j];
+                if (x > top1) { top3 = top2; top2 = top1; top1 = x; }
+                else if (x > top2) { top3 = top2; top2 = x; }
+                else if (x > top3) { top3 = x; }
+              }
               mybuf_s[nb] = v[j];
               mybuf_r[nb] = r;
               ++nb;
@@ -332,8 +419,17 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(acc_empty + a);
+      if (fast_pub && valid_q) {
+        const float xj = p.jth == 1 ? top1 : (p.jth == 2 ? top2 : top3);
+        const uint32_t key = xj == -INFINITY ? 0u : score_key(xj);
+        if (key > published) {
+          published = key;
+          p.pub[size_t(slice * 2 + chalf) * p.n_queries + qi] = key;
+        }
+      }
     }
     flush(1);
+    if (lane == 0) atomicAdd(s_done, 1u);
     // Coalesced copy of each lane's final list into this slice's output.
     for (uint32_t f = 0; f < 32; ++f) {
       const uint32_t fq = qt * BM + quarter * 32 + f;
@@ -342,7 +438,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t f_half = __shfl_sync(0xFFFFFFFFu, half, f);
       const float* ls = Lw_s + (size_t(f) * 2 + f_half) * p.k;
       const uint32_t* lr = Lw_r + (size_t(f) * 2 + f_half) * p.k;
-      const size_t base = (size_t(slice) * p.n_queries + fq) * p.k;
+      const size_t base = ((size_t(slice) * 2 + chalf) * p.n_queries + fq) * p.k;
       for (uint32_t i = lane; i < p.k; i += 32) {
         p.part_s[base + i] = i < f_cnt ? ls[i] : -INFINITY;
         p.part_id[base + i] = i < f_cnt ? int64_t(lr[i]) + int64_t(p.row_offset) : int64_t(-1);
@@ -587,9 +683,12 @@ extern "C" int cr_filtered_topk(const uint16_t* d_db, const float* d_db_norms, u
   const bool l2 = metric == CR_METRIC_L2;
 
   const size_t ctas = size_t(qtiles) * slices;
-  const size_t list_b = ctas * 2 * k * BM * 4;
-  const size_t part_b = size_t(slices) * n_queries * k;
-  Scratch scr(list_b * 2 + part_b * 12 + (filter ? pass_words * 4 : 0) +
+  const size_t list_b = ctas * 2 * 2 * k * BM * 4;
+  const size_t part_b = size_t(slices) * 2 * n_queries * k;
+  const size_t cbuf_b = ctas * EPI * BUF * 4;
+  const uint32_t n_lists = slices * 2;
+  const size_t pub_b = size_t(n_queries) * n_lists * 4;
+  Scratch scr(list_b * 2 + cbuf_b * 2 + part_b * 12 + pub_b + (filter ? pass_words * 4 : 0) +
                   ((l2 && !d_db_norms) ? n_rows * 4 : 0) + size_t(n_queries) * 4 + 64 + 256,
               s);
   char* p = scr.as<char>();
@@ -603,6 +702,12 @@ extern "C" int cr_filtered_topk(const uint16_t* d_db, const float* d_db_norms, u
   tp.row_offset = row_offset;
   tp.list_s = reinterpret_cast<float*>(p); p += list_b;
   tp.list_r = reinterpret_cast<uint32_t*>(p); p += list_b;
+  tp.buf_s = reinterpret_cast<float*>(p); p += cbuf_b;
+  tp.buf_r = reinterpret_cast<uint32_t*>(p); p += cbuf_b;
+  tp.pub = reinterpret_cast<uint32_t*>(p); p += pub_b;
+  tp.n_lists = n_lists;
+  tp.jth = (k + n_lists - 1) / n_lists;
+  CR_CUDA(cudaMemsetAsync(tp.pub, 0, pub_b, s));
   tp.part_id = reinterpret_cast<int64_t*>(p); p += part_b * 8;
   tp.part_s = reinterpret_cast<float*>(p); p += part_b * 4;
   p = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(p) + 15) & ~uintptr_t(15));
@@ -629,6 +734,7 @@ extern "C" int cr_filtered_topk(const uint16_t* d_db, const float* d_db_norms, u
   p = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(p) + 15) & ~uintptr_t(15));
   tp.err = reinterpret_cast<uint32_t*>(p);
   tp.shared_thr = tp.err + 4;
+  if (const char* dbg = getenv("CR_TOPK_DEBUG")) tp.debug = uint32_t(atoi(dbg));
   CR_CUDA(cudaMemsetAsync(tp.err, 0, 16 + size_t(n_queries) * 4, s));
   const CUtensorMap tq = make_map(d_queries, n_queries, BM);
   const CUtensorMap tdb = make_map(d_db, n_rows, BN);
@@ -637,11 +743,17 @@ extern "C" int cr_filtered_topk(const uint16_t* d_db, const float* d_db_norms, u
     k_topk<<<dim3(qtiles, slices), THREADS, SMEM_TOTAL, s>>>(tq, tdb, tp);
   }
   CR_CUDA(cudaGetLastError());
-  merge_launch(tp.part_s, tp.part_id, slices, n_queries, k, metric, 0,
+  merge_launch(tp.part_s, tp.part_id, slices * 2, n_queries, k, metric, 0,
                reinterpret_cast<const __half*>(d_queries), dim, d_out_dist, d_out_ids, s);
   uint32_t h_err = 0;
   CR_CUDA(cudaMemcpyAsync(&h_err, tp.err, 4, cudaMemcpyDeviceToHost, s));
   CR_CUDA(cudaStreamSynchronize(s));
+  if (tp.debug == 3) {
+    uint32_t c[4];
+    CR_CUDA(cudaMemcpy(c, tp.err, 16, cudaMemcpyDeviceToHost));
+    fprintf(stderr, "topk debug: lane flushes %u, warp flush rounds %u, inserts %u\n", c[1], c[2], c[3]);
+    h_err = c[0];
+  }
   if (h_err) fail(CR_ERR_DEVICE, "cr_filtered_topk: pipeline wait timed out (code " + std::to_string(h_err) + ")");
   CR_API_END
 }
