@@ -31,6 +31,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <mutex>
+#include <vector>
 
 #include "chunk_ops.cuh"
 #include "cu_roaring/device/make_view.cuh"
@@ -82,6 +83,7 @@ struct TopkParams {
   uint32_t* pub;         // [Q][n_lists] published j-th best of every partial list (score keys)
   uint32_t n_lists;      // partial lists per query (2 per slice)
   uint32_t jth;          // ceil(k / n_lists)
+  const uint32_t* row_map;  // compacted row -> shard row (null: identity)
 };
 
 // Order-preserving map float -> uint32 (larger float -> larger key); 0 is
@@ -441,7 +443,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       const size_t base = ((size_t(slice) * 2 + chalf) * p.n_queries + fq) * p.k;
       for (uint32_t i = lane; i < p.k; i += 32) {
         p.part_s[base + i] = i < f_cnt ? ls[i] : -INFINITY;
-        p.part_id[base + i] = i < f_cnt ? int64_t(lr[i]) + int64_t(p.row_offset) : int64_t(-1);
+        const uint32_t r = i < f_cnt ? lr[i] : 0u;
+        p.part_id[base + i] =
+            i < f_cnt ? int64_t(p.row_map ? __ldg(p.row_map + r) : r) + int64_t(p.row_offset) : int64_t(-1);
       }
     }
   }
@@ -576,6 +580,64 @@ __global__ void k_row_norms(const uint4* db, uint64_t n_rows, float* out)
   if (row < n_rows && sub == 0) out[row] = acc;
 }
 
+// -------------------------------------------------- pre-filter compaction
+constexpr uint32_t kWordTile = 1024;
+
+__global__ void __launch_bounds__(kWordTile) k_pass_tile_sums(const uint32_t* pass, uint64_t n_words,
+                                                              uint32_t* tile_sums)
+{
+  __shared__ uint32_t s_red[32];
+  const uint64_t w = uint64_t(blockIdx.x) * kWordTile + threadIdx.x;
+  const uint32_t c = w < n_words ? __popc(pass[w]) : 0u;
+  const uint32_t t = block_sum<kWordTile>(c, s_red);
+  if (threadIdx.x == 0) tile_sums[blockIdx.x] = t;
+}
+
+// idx[] = shard rows whose filter bit is set, ascending; *total = count.
+__global__ void __launch_bounds__(kWordTile) k_pass_compact(const uint32_t* pass, uint64_t n_words,
+                                                            const uint32_t* tile_sums, uint32_t n_tiles,
+                                                            uint32_t* idx, uint32_t* total)
+{
+  __shared__ uint32_t s_red[32];
+  __shared__ uint32_t s_base;
+  if (threadIdx.x == 0) {
+    uint32_t b = 0, all = 0;
+    for (uint32_t j = 0; j < n_tiles; ++j) {
+      if (j < blockIdx.x) b += tile_sums[j];
+      all += tile_sums[j];
+    }
+    s_base = b;
+    if (blockIdx.x == 0) *total = all;
+  }
+  __syncthreads();
+  const uint64_t w = uint64_t(blockIdx.x) * kWordTile + threadIdx.x;
+  uint32_t x = w < n_words ? pass[w] : 0u;
+  uint32_t tot;
+  uint32_t pos = s_base + block_exclusive_scan<kWordTile>(uint32_t(__popc(x)), s_red, &tot);
+  while (x) {
+    idx[pos++] = uint32_t(w * 32 + __ffs(x) - 1);
+    x &= x - 1;
+  }
+}
+
+// comp[i] = db[idx[i]] (16 lanes x 16 B per 128-dim row); norms likewise.
+__global__ void k_gather_rows(const uint4* db, const uint32_t* idx, uint32_t n, uint4* comp,
+                              const float* norms, float* comp_norms)
+{
+  const uint64_t g = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const uint64_t row = g >> 4;
+  if (row >= n) return;
+  const uint32_t src = __ldg(idx + row);
+  comp[row * 16 + (g & 15)] = __ldcs(db + uint64_t(src) * 16 + (g & 15));
+  if (norms && (g & 15) == 0) comp_norms[row] = __ldg(norms + src);
+}
+
+__global__ void k_fill_empty(float* d, int64_t* ids, uint64_t n, float v)
+{
+  const uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n) { d[i] = v; ids[i] = -1; }
+}
+
 // ------------------------------------------------------------------- host
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
@@ -651,6 +713,77 @@ extern "C" int cr_row_norms(const uint16_t* d_db, uint64_t n_rows, uint32_t dim,
   CR_API_END
 }
 
+// The tcgen05 search over `n_rows` rows (optionally masked by `pass`, row
+// ids optionally translated by `row_map`) plus the per-query merge.
+static void run_topk_core(const uint16_t* d_db, const float* norms, uint64_t n_rows, const uint32_t* pass,
+                          const uint32_t* row_map, const uint16_t* d_queries, uint32_t n_queries,
+                          uint64_t row_offset, uint32_t k, int metric, float* d_out_dist,
+                          int64_t* d_out_ids, cudaStream_t s)
+{
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaFuncSetAttribute(k_topk, cudaFuncAttributeMaxDynamicSharedMemorySize, int(SMEM_TOTAL));
+  });
+  const uint32_t n_tiles = div_up(n_rows, BN);
+  const uint32_t qtiles = div_up(n_queries, BM);
+  const uint32_t want_slices = std::max(1, sm_count() / int(qtiles));
+  const uint32_t tps = div_up(n_tiles, std::min<uint32_t>(want_slices, n_tiles));
+  const uint32_t slices = div_up(n_tiles, tps);
+  const size_t ctas = size_t(qtiles) * slices;
+  const size_t list_b = ctas * 2 * 2 * k * BM * 4;
+  const size_t part_b = size_t(slices) * 2 * n_queries * k;
+  const size_t cbuf_b = ctas * EPI * BUF * 4;
+  const uint32_t n_lists = slices * 2;
+  const size_t pub_b = size_t(n_queries) * n_lists * 4;
+  Scratch scr(list_b * 2 + cbuf_b * 2 + part_b * 12 + pub_b + size_t(n_queries) * 4 + 64 + 256, s);
+  char* p = scr.as<char>();
+  TopkParams tp{};
+  tp.n_rows = static_cast<uint32_t>(n_rows);
+  tp.n_queries = n_queries;
+  tp.k = k;
+  tp.metric = metric;
+  tp.n_tiles = n_tiles;
+  tp.tiles_per_slice = tps;
+  tp.row_offset = row_offset;
+  tp.pass = pass;
+  tp.norms = norms;
+  tp.row_map = row_map;
+  tp.list_s = reinterpret_cast<float*>(p); p += list_b;
+  tp.list_r = reinterpret_cast<uint32_t*>(p); p += list_b;
+  tp.buf_s = reinterpret_cast<float*>(p); p += cbuf_b;
+  tp.buf_r = reinterpret_cast<uint32_t*>(p); p += cbuf_b;
+  tp.pub = reinterpret_cast<uint32_t*>(p); p += pub_b;
+  tp.n_lists = n_lists;
+  tp.jth = (k + n_lists - 1) / n_lists;
+  CR_CUDA(cudaMemsetAsync(tp.pub, 0, pub_b, s));
+  tp.part_id = reinterpret_cast<int64_t*>(p); p += part_b * 8;
+  tp.part_s = reinterpret_cast<float*>(p); p += part_b * 4;
+  p = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(p) + 15) & ~uintptr_t(15));
+  tp.err = reinterpret_cast<uint32_t*>(p);
+  tp.shared_thr = tp.err + 4;
+  if (const char* dbg = getenv("CR_TOPK_DEBUG")) tp.debug = uint32_t(atoi(dbg));
+  CR_CUDA(cudaMemsetAsync(tp.err, 0, 16 + size_t(n_queries) * 4, s));
+  const CUtensorMap tq = make_map(d_queries, n_queries, BM);
+  const CUtensorMap tdb = make_map(d_db, n_rows, BN);
+  {
+    ProfileScope prof(CR_KERNEL_TOPK, s);
+    k_topk<<<dim3(qtiles, slices), THREADS, SMEM_TOTAL, s>>>(tq, tdb, tp);
+  }
+  CR_CUDA(cudaGetLastError());
+  merge_launch(tp.part_s, tp.part_id, slices * 2, n_queries, k, metric, 0,
+               reinterpret_cast<const __half*>(d_queries), DIM, d_out_dist, d_out_ids, s);
+  uint32_t h_err = 0;
+  CR_CUDA(cudaMemcpyAsync(&h_err, tp.err, 4, cudaMemcpyDeviceToHost, s));
+  CR_CUDA(cudaStreamSynchronize(s));
+  if (tp.debug == 3) {
+    uint32_t c[4];
+    CR_CUDA(cudaMemcpy(c, tp.err, 16, cudaMemcpyDeviceToHost));
+    fprintf(stderr, "topk debug: lane flushes %u, warp flush rounds %u, inserts %u\n", c[1], c[2], c[3]);
+    h_err = c[0];
+  }
+  if (h_err) fail(CR_ERR_DEVICE, "cr_filtered_topk: pipeline wait timed out (code " + std::to_string(h_err) + ")");
+}
+
 extern "C" int cr_filtered_topk(const uint16_t* d_db, const float* d_db_norms, uint64_t n_rows,
                                 uint32_t dim, const uint16_t* d_queries, uint32_t n_queries,
                                 const cr_gpu_roaring* filter, uint64_t row_offset, uint32_t k,
@@ -668,93 +801,70 @@ extern "C" int cr_filtered_topk(const uint16_t* d_db, const float* d_db_norms, u
                  (reinterpret_cast<uintptr_t>(d_queries) & 15u) == 0,
              "cr_filtered_topk: db and queries must be 16-byte aligned");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-
-  static std::once_flag once;
-  std::call_once(once, [] {
-    cudaFuncSetAttribute(k_topk, cudaFuncAttributeMaxDynamicSharedMemorySize, int(SMEM_TOTAL));
-  });
-
-  const uint32_t n_tiles = div_up(n_rows, BN);
-  const uint32_t qtiles = div_up(n_queries, BM);
-  const uint32_t want_slices = std::max(1, sm_count() / int(qtiles));
-  const uint32_t tps = div_up(n_tiles, std::min<uint32_t>(want_slices, n_tiles));
-  const uint32_t slices = div_up(n_tiles, tps);
-  const uint64_t pass_words = (n_rows + 31) / 32 + 1;
   const bool l2 = metric == CR_METRIC_L2;
 
-  const size_t ctas = size_t(qtiles) * slices;
-  const size_t list_b = ctas * 2 * 2 * k * BM * 4;
-  const size_t part_b = size_t(slices) * 2 * n_queries * k;
-  const size_t cbuf_b = ctas * EPI * BUF * 4;
-  const uint32_t n_lists = slices * 2;
-  const size_t pub_b = size_t(n_queries) * n_lists * 4;
-  Scratch scr(list_b * 2 + cbuf_b * 2 + part_b * 12 + pub_b + (filter ? pass_words * 4 : 0) +
-                  ((l2 && !d_db_norms) ? n_rows * 4 : 0) + size_t(n_queries) * 4 + 64 + 256,
-              s);
-  char* p = scr.as<char>();
-  TopkParams tp{};
-  tp.n_rows = static_cast<uint32_t>(n_rows);
-  tp.n_queries = n_queries;
-  tp.k = k;
-  tp.metric = metric;
-  tp.n_tiles = n_tiles;
-  tp.tiles_per_slice = tps;
-  tp.row_offset = row_offset;
-  tp.list_s = reinterpret_cast<float*>(p); p += list_b;
-  tp.list_r = reinterpret_cast<uint32_t*>(p); p += list_b;
-  tp.buf_s = reinterpret_cast<float*>(p); p += cbuf_b;
-  tp.buf_r = reinterpret_cast<uint32_t*>(p); p += cbuf_b;
-  tp.pub = reinterpret_cast<uint32_t*>(p); p += pub_b;
-  tp.n_lists = n_lists;
-  tp.jth = (k + n_lists - 1) / n_lists;
-  CR_CUDA(cudaMemsetAsync(tp.pub, 0, pub_b, s));
-  tp.part_id = reinterpret_cast<int64_t*>(p); p += part_b * 8;
-  tp.part_s = reinterpret_cast<float*>(p); p += part_b * 4;
-  p = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(p) + 15) & ~uintptr_t(15));
-  if (filter) {
-    uint32_t* pass = reinterpret_cast<uint32_t*>(p);
-    p += pass_words * 4;
+  // Squared norms of the shard rows (L2 only), computed here when not given.
+  Scratch norm_scr((l2 && !d_db_norms) ? n_rows * 4 : 0, s);
+  const float* norms = d_db_norms;
+  if (l2 && !norms) {
+    row_norms(d_db, n_rows, norm_scr.as<float>(), s);
+    norms = norm_scr.as<float>();
+  }
+  if (!filter) {
+    run_topk_core(d_db, norms, n_rows, nullptr, nullptr, d_queries, n_queries, row_offset, k, metric,
+                  d_out_dist, d_out_ids, s);
+    return CR_OK;
+  }
+  // Shard-local pass bitset from the Roaring filter.
+  const uint64_t pass_words = (n_rows + 31) / 32;
+  const uint32_t n_wtiles = div_up(pass_words, kWordTile);
+  Scratch pass_scr(pass_words * 4 + 16 + size_t(n_wtiles) * 4 + 16, s);
+  uint32_t* pass = pass_scr.as<uint32_t>();
+  uint32_t* d_total = pass + pass_words;
+  uint32_t* tiles = d_total + 4;
+  {
     const cu_roaring::GpuRoaringView v =
         cu_roaring::make_view(*reinterpret_cast<const cu_roaring::GpuRoaring*>(filter));
     const uint64_t threads = pass_words * 32;
     const int grid = static_cast<int>(std::min<uint64_t>(div_up(threads, 256), uint64_t(sm_count()) * 16));
     k_pass_bits<<<grid, 256, 0, s>>>(v, row_offset, n_rows, pass, pass_words);
-    tp.pass = pass;
   }
-  if (l2) {
-    if (d_db_norms) {
-      tp.norms = d_db_norms;
-    } else {
-      float* nrm = reinterpret_cast<float*>(p);
-      p += n_rows * 4;
-      row_norms(d_db, n_rows, nrm, s);
-      tp.norms = nrm;
-    }
-  }
-  p = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(p) + 15) & ~uintptr_t(15));
-  tp.err = reinterpret_cast<uint32_t*>(p);
-  tp.shared_thr = tp.err + 4;
-  if (const char* dbg = getenv("CR_TOPK_DEBUG")) tp.debug = uint32_t(atoi(dbg));
-  CR_CUDA(cudaMemsetAsync(tp.err, 0, 16 + size_t(n_queries) * 4, s));
-  const CUtensorMap tq = make_map(d_queries, n_queries, BM);
-  const CUtensorMap tdb = make_map(d_db, n_rows, BN);
-  {
-    ProfileScope prof(CR_KERNEL_TOPK, s);
-    k_topk<<<dim3(qtiles, slices), THREADS, SMEM_TOTAL, s>>>(tq, tdb, tp);
-  }
+  k_pass_tile_sums<<<n_wtiles, kWordTile, 0, s>>>(pass, pass_words, tiles);
   CR_CUDA(cudaGetLastError());
-  merge_launch(tp.part_s, tp.part_id, slices * 2, n_queries, k, metric, 0,
-               reinterpret_cast<const __half*>(d_queries), dim, d_out_dist, d_out_ids, s);
-  uint32_t h_err = 0;
-  CR_CUDA(cudaMemcpyAsync(&h_err, tp.err, 4, cudaMemcpyDeviceToHost, s));
-  CR_CUDA(cudaStreamSynchronize(s));
-  if (tp.debug == 3) {
-    uint32_t c[4];
-    CR_CUDA(cudaMemcpy(c, tp.err, 16, cudaMemcpyDeviceToHost));
-    fprintf(stderr, "topk debug: lane flushes %u, warp flush rounds %u, inserts %u\n", c[1], c[2], c[3]);
-    h_err = c[0];
+  // Count first: the compacted copy is only worth it below half density.
+  uint32_t h_tiles_total = 0;
+  {
+    std::vector<uint32_t> h(n_wtiles);
+    CR_CUDA(cudaMemcpyAsync(h.data(), tiles, n_wtiles * 4, cudaMemcpyDeviceToHost, s));
+    CR_CUDA(cudaStreamSynchronize(s));
+    for (uint32_t x : h) h_tiles_total += x;
   }
-  if (h_err) fail(CR_ERR_DEVICE, "cr_filtered_topk: pipeline wait timed out (code " + std::to_string(h_err) + ")");
+  const uint32_t n_pass = h_tiles_total;
+  if (n_pass == 0) {
+    const uint64_t n = uint64_t(n_queries) * k;
+    k_fill_empty<<<div_up(n, 256), 256, 0, s>>>(d_out_dist, d_out_ids, n, l2 ? INFINITY : -INFINITY);
+    CR_CUDA(cudaGetLastError());
+    return CR_OK;
+  }
+  if (uint64_t(n_pass) * 2 > n_rows) {
+    // Dense rows with the predicate applied per 32-row chunk in the epilogue.
+    run_topk_core(d_db, norms, n_rows, pass, nullptr, d_queries, n_queries, row_offset, k, metric,
+                  d_out_dist, d_out_ids, s);
+    return CR_OK;
+  }
+  // Pre-filter: gather the passing rows into a dense copy and search that.
+  Scratch comp_scr(size_t(n_pass) * 4 + 256 + size_t(n_pass) * DIM * 2 + (l2 ? size_t(n_pass) * 4 + 16 : 0), s);
+  uint32_t* idx = comp_scr.as<uint32_t>();
+  uint16_t* comp = reinterpret_cast<uint16_t*>(
+      (reinterpret_cast<uintptr_t>(idx + n_pass) + 255) & ~uintptr_t(255));
+  float* comp_norms = l2 ? reinterpret_cast<float*>(comp + size_t(n_pass) * DIM) : nullptr;
+  k_pass_compact<<<n_wtiles, kWordTile, 0, s>>>(pass, pass_words, tiles, n_wtiles, idx, d_total);
+  k_gather_rows<<<div_up(uint64_t(n_pass) * 16, 256), 256, 0, s>>>(
+      reinterpret_cast<const uint4*>(d_db), idx, n_pass, reinterpret_cast<uint4*>(comp), l2 ? norms : nullptr,
+      comp_norms);
+  CR_CUDA(cudaGetLastError());
+  run_topk_core(comp, comp_norms, n_pass, nullptr, idx, d_queries, n_queries, row_offset, k, metric,
+                d_out_dist, d_out_ids, s);
   CR_API_END
 }
 

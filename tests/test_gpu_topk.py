@@ -113,3 +113,15 @@ def test_topk_against_torch_fp32_large(cr, torch_):
     ref_d, ref_i = torch_.topk(scores, k, dim=1)
     check_topk(d.cpu().numpy(), i.cpu().numpy(), ref_d.cpu().numpy(), ref_i.cpu().numpy(), 0)
     filt.free()
+
+
+def test_topk_no_passing_rows(cr, torch_):
+    """A filter that excludes every row of the shard: every slot is (inf/-inf, -1)."""
+    db, qs = make_data(4096, 20, seed=2)
+    filt = cr.upload_from_ids(np.array([5000, 6000], np.uint32), 10000)  # rows outside [0, 4096)
+    for metric in (0, 1):
+        d, i = cr.filtered_topk(torch_.from_numpy(db).cuda(), torch_.from_numpy(qs).cuda(), 7, metric=metric,
+                                filter=filt)
+        assert (i.cpu().numpy() == -1).all()
+        assert np.isinf(d.cpu().numpy()).all()
+    filt.free()
