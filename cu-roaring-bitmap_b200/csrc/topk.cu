@@ -84,7 +84,14 @@ struct TopkParams {
   uint32_t n_lists;      // partial lists per query (2 per slice)
   uint32_t jth;          // ceil(k / n_lists)
   const uint32_t* row_map;  // compacted row -> shard row (null: identity)
+  uint32_t append;       // 1: survivors go to per-query candidate arrays, no list merges
+  uint32_t cap;          // candidate slots per query (append mode)
+  float* cand_s;         // [Q][cap]
+  uint32_t* cand_r;
+  uint32_t* cand_cnt;    // [Q]
 };
+
+constexpr uint32_t kErrOverflow = 64u;  // a candidate array filled up (append mode)
 
 // Order-preserving map float -> uint32 (larger float -> larger key); 0 is
 // below every real score and decodes to -inf.
@@ -384,7 +391,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         tmem_ld32(tmem + ((quarter * 32u) << 16) + a * BN + c * 32, v);
         if (l2) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = 2.f * v[j] - __ldg(p.norms + r0 + j);
+          for (int j = 0; j < 32; ++j)  // rows past the mask (and n_rows) are never read
+            v[j] = ((m >> j) & 1u) ? 2.f * v[j] - __ldg(p.norms + r0 + j) : -INFINITY;
         }
         // Fast path: the best passing score of the chunk against the bound.
         float mx = -INFINITY;
@@ -398,6 +406,31 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int j = 0; j < 32; ++j) cm |= (v[j] >= bound ? 1u : 0u) << j;
           cm &= valid_q ? m : 0u;
           const uint32_t any = __reduce_or_sync(0xFFFFFFFFu, cm);
+          if (p.append) {
+            // One reservation per lane per chunk, then rank-ordered stores.
+            const uint32_t n_ins = __popc(cm);
+            uint32_t base = 0;
+            if (n_ins) base = atomicAdd(p.cand_cnt + qi, n_ins);
+            const bool fits = base + n_ins <= p.cap;
+            if (n_ins && !fits) atomicOr(p.err, kErrOverflow);
+            const size_t qb = size_t(qi) * p.cap;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if (!((any >> j) & 1u)) continue;
+              if ((cm >> j) & 1u) {
+                const float x = v[j];
+                if (fits) {
+                  const uint32_t at = base + __popc(cm & ((1u << j) - 1u));
+                  p.cand_s[qb + at] = x;
+                  p.cand_r[qb + at] = r0 + j;
+                }
+                if (x > top1) { top3 = top2; top2 = top1; top1 = x; }
+                else if (x > top2) { top3 = top2; top2 = x; }
+                else if (x > top3) { top3 = x; }
+              }
+            }
+            continue;
+          }
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             if (!((any >> j) & 1u)) continue;
@@ -433,7 +466,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     flush(1);
     if (lane == 0) atomicAdd(s_done, 1u);
     // Coalesced copy of each lane's final list into this slice's output.
-    for (uint32_t f = 0; f < 32; ++f) {
+    for (uint32_t f = 0; f < (p.append ? 0u : 32u); ++f) {
       const uint32_t fq = qt * BM + quarter * 32 + f;
       if (fq >= p.n_queries) break;
       const uint32_t f_cnt = __shfl_sync(0xFFFFFFFFu, cnt, f);
@@ -489,7 +522,12 @@ __global__ void __launch_bounds__(MERGE_THREADS) k_merge(const float* part_s, co
                                                          uint32_t parts, uint32_t n_queries,
                                                          uint32_t k, int metric, int kind,
                                                          const __half* queries, uint32_t dim,
-                                                         float* out_d, int64_t* out_id)
+                                                         float* out_d, int64_t* out_id,
+                                                         const uint32_t* cand_cnt, uint32_t cap,
+                                                         const uint32_t* cand_r,
+                                                         const uint32_t* row_map, uint64_t row_offset,
+                                                         const uint32_t* pub, uint32_t n_lists,
+                                                         uint32_t n_rows)
 {
   extern __shared__ uint8_t smem_raw[];
   float* s = reinterpret_cast<float*>(smem_raw);
@@ -499,7 +537,7 @@ __global__ void __launch_bounds__(MERGE_THREADS) k_merge(const float* part_s, co
   const bool l2 = metric == CR_METRIC_L2;
   if (threadIdx.x < 32) {
     float acc = 0.f;
-    if (l2 && kind == 0)
+    if (l2 && kind != 1)
       for (uint32_t d = threadIdx.x; d < dim; d += 32) {
         const float x = __half2float(queries[size_t(q) * dim + d]);
         acc += x * x;
@@ -508,11 +546,36 @@ __global__ void __launch_bounds__(MERGE_THREADS) k_merge(const float* part_s, co
     for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
     if (threadIdx.x == 0) s_qn = acc;
   }
-  const uint64_t total = uint64_t(parts) * k;
+  // kind 2 (candidate arrays): only candidates at or above the final
+  // published bound (min over lists of their jth best) can be in the top k.
+  float bound = -INFINITY;
+  if (kind == 2 && pub) {
+    __shared__ uint32_t s_min;
+    if (threadIdx.x == 0) s_min = 0xFFFFFFFFu;
+    __syncthreads();
+    uint32_t mn = 0xFFFFFFFFu;
+    for (uint32_t l = threadIdx.x; l < n_lists; l += MERGE_THREADS) mn = min(mn, pub[size_t(l) * n_queries + q]);
+    atomicMin(&s_min, mn);
+    __syncthreads();
+    bound = key_score(s_min);
+  }
+  // An overflowed candidate array has unwritten slots; that pass is redone
+  // by the caller, so the query is skipped here.
+  const uint64_t total = kind == 2 ? (cand_cnt[q] > cap ? 0u : cand_cnt[q]) : uint64_t(parts) * k;
   auto load = [&](uint64_t c, uint32_t slot) {
     float v = -INFINITY;
     int64_t i = -1;
-    if (c < total) {
+    if (kind == 2) {
+      if (c < total) {
+        const size_t g = size_t(q) * cap + c;
+        const float x = part_s[g];
+        if (x >= bound) {
+          const uint32_t r = cand_r[g];
+          v = x;
+          i = int64_t(row_map ? __ldg(row_map + r) : r) + int64_t(row_offset);
+        }
+      }
+    } else if (c < total) {
       const uint32_t pidx = static_cast<uint32_t>(c / k), e = static_cast<uint32_t>(c % k);
       const size_t g = (size_t(pidx) * n_queries + q) * k + e;
       i = part_id[g];
@@ -522,16 +585,49 @@ __global__ void __launch_bounds__(MERGE_THREADS) k_merge(const float* part_s, co
     s[slot] = v;
     id[slot] = i;
   };
-  uint64_t pos = 0;
-  for (uint32_t i = threadIdx.x; i < MERGE_N; i += MERGE_THREADS) load(pos + i, i);
-  pos += MERGE_N;
-  __syncthreads();
-  bitonic_sort(s, id);
-  while (pos < total) {
-    for (uint32_t i = k + threadIdx.x; i < MERGE_N; i += MERGE_THREADS) load(pos + (i - k), i);
-    pos += MERGE_N - k;
+  if (kind == 2) {
+    // Stream the candidates; only those at or above the bound are kept,
+    // compacted into the free slots [k, MERGE_N), sorted when full.
+    __shared__ uint32_t s_fill;
+    for (uint32_t i = threadIdx.x; i < MERGE_N; i += MERGE_THREADS) { s[i] = -INFINITY; id[i] = -1; }
+    if (threadIdx.x == 0) s_fill = 0;
+    __syncthreads();
+    constexpr uint32_t B = 2 * MERGE_THREADS;
+    for (uint64_t c0 = 0; c0 < total; c0 += B) {
+      if (s_fill + B > MERGE_N - k) {
+        bitonic_sort(s, id);
+        for (uint32_t i = k + threadIdx.x; i < MERGE_N; i += MERGE_THREADS) { s[i] = -INFINITY; id[i] = -1; }
+        __syncthreads();
+        if (threadIdx.x == 0) s_fill = 0;
+        __syncthreads();
+      }
+      for (uint32_t j = threadIdx.x; j < B; j += MERGE_THREADS) {
+        const uint64_t c = c0 + j;
+        if (c >= total) break;
+        const size_t g = size_t(q) * cap + c;
+        const float x = part_s[g];
+        const uint32_t r = cand_r[g];
+        if (x >= bound && r < n_rows) {
+          const uint32_t slot = k + atomicAdd(&s_fill, 1u);
+          s[slot] = x;
+          id[slot] = int64_t(row_map ? __ldg(row_map + r) : r) + int64_t(row_offset);
+        }
+      }
+      __syncthreads();
+    }
+    bitonic_sort(s, id);
+  } else {
+    uint64_t pos = 0;
+    for (uint32_t i = threadIdx.x; i < MERGE_N; i += MERGE_THREADS) load(pos + i, i);
+    pos += MERGE_N;
     __syncthreads();
     bitonic_sort(s, id);
+    while (pos < total) {
+      for (uint32_t i = k + threadIdx.x; i < MERGE_N; i += MERGE_THREADS) load(pos + (i - k), i);
+      pos += MERGE_N - k;
+      __syncthreads();
+      bitonic_sort(s, id);
+    }
   }
   const float qn = s_qn;
   for (uint32_t i = threadIdx.x; i < k; i += MERGE_THREADS) {
@@ -539,7 +635,7 @@ __global__ void __launch_bounds__(MERGE_THREADS) k_merge(const float* part_s, co
     float d;
     if (r < 0) d = l2 ? INFINITY : -INFINITY;
     else if (!l2) d = s[i];
-    else d = (kind == 0) ? qn - s[i] : -s[i];
+    else d = (kind != 1) ? qn - s[i] : -s[i];
     out_d[size_t(q) * k + i] = d;
     out_id[size_t(q) * k + i] = r;
   }
@@ -679,14 +775,18 @@ CUtensorMap make_map(const void* base, uint64_t rows, uint32_t box_rows)
 
 void merge_launch(const float* ps, const int64_t* pid, uint32_t parts, uint32_t nq, uint32_t k,
                   int metric, int kind, const __half* queries, uint32_t dim, float* od, int64_t* oi,
-                  cudaStream_t s)
+                  cudaStream_t s, const uint32_t* cand_cnt = nullptr, uint32_t cap = 0,
+                  const uint32_t* cand_r = nullptr, const uint32_t* row_map = nullptr,
+                  uint64_t row_offset = 0, const uint32_t* pub = nullptr, uint32_t n_lists = 0,
+                  uint32_t n_rows = 0)
 {
   static std::once_flag once;
   const size_t smem = MERGE_N * 12;
   std::call_once(once, [&] {
     cudaFuncSetAttribute(k_merge, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   });
-  k_merge<<<nq, MERGE_THREADS, smem, s>>>(ps, pid, parts, nq, k, metric, kind, queries, dim, od, oi);
+  k_merge<<<nq, MERGE_THREADS, smem, s>>>(ps, pid, parts, nq, k, metric, kind, queries, dim, od, oi,
+                                          cand_cnt, cap, cand_r, row_map, row_offset, pub, n_lists, n_rows);
   CR_CUDA(cudaGetLastError());
 }
 
@@ -718,7 +818,7 @@ extern "C" int cr_row_norms(const uint16_t* d_db, uint64_t n_rows, uint32_t dim,
 static void run_topk_core(const uint16_t* d_db, const float* norms, uint64_t n_rows, const uint32_t* pass,
                           const uint32_t* row_map, const uint16_t* d_queries, uint32_t n_queries,
                           uint64_t row_offset, uint32_t k, int metric, float* d_out_dist,
-                          int64_t* d_out_ids, cudaStream_t s)
+                          int64_t* d_out_ids, cudaStream_t s, bool allow_append = true)
 {
   static std::once_flag once;
   std::call_once(once, [] {
@@ -735,7 +835,13 @@ static void run_topk_core(const uint16_t* d_db, const float* norms, uint64_t n_r
   const size_t cbuf_b = ctas * EPI * BUF * 4;
   const uint32_t n_lists = slices * 2;
   const size_t pub_b = size_t(n_queries) * n_lists * 4;
-  Scratch scr(list_b * 2 + cbuf_b * 2 + part_b * 12 + pub_b + size_t(n_queries) * 4 + 64 + 256, s);
+  const uint32_t jth = (k + n_lists - 1) / n_lists;
+  // Append mode needs the register-tracked list bounds (jth <= 3); its
+  // candidate arrays hold up to `cap` survivors per query.
+  const bool append = allow_append && jth <= 3;
+  const uint32_t cap = append ? std::max<uint32_t>(32768u, 128u * k) : 0u;
+  const size_t cand_b = append ? size_t(n_queries) * cap * 4 : 0;
+  Scratch scr(list_b * 2 + cbuf_b * 2 + part_b * 12 + pub_b + cand_b * 2 + size_t(n_queries) * 8 + 64 + 512, s);
   char* p = scr.as<char>();
   TopkParams tp{};
   tp.n_rows = static_cast<uint32_t>(n_rows);
@@ -754,8 +860,16 @@ static void run_topk_core(const uint16_t* d_db, const float* norms, uint64_t n_r
   tp.buf_r = reinterpret_cast<uint32_t*>(p); p += cbuf_b;
   tp.pub = reinterpret_cast<uint32_t*>(p); p += pub_b;
   tp.n_lists = n_lists;
-  tp.jth = (k + n_lists - 1) / n_lists;
+  tp.jth = jth;
   CR_CUDA(cudaMemsetAsync(tp.pub, 0, pub_b, s));
+  tp.append = append ? 1u : 0u;
+  tp.cap = cap;
+  if (append) {
+    tp.cand_s = reinterpret_cast<float*>(p); p += cand_b;
+    tp.cand_r = reinterpret_cast<uint32_t*>(p); p += cand_b;
+    tp.cand_cnt = reinterpret_cast<uint32_t*>(p); p += size_t(n_queries) * 4;
+    CR_CUDA(cudaMemsetAsync(tp.cand_cnt, 0, size_t(n_queries) * 4, s));
+  }
   tp.part_id = reinterpret_cast<int64_t*>(p); p += part_b * 8;
   tp.part_s = reinterpret_cast<float*>(p); p += part_b * 4;
   p = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(p) + 15) & ~uintptr_t(15));
@@ -770,8 +884,13 @@ static void run_topk_core(const uint16_t* d_db, const float* norms, uint64_t n_r
     k_topk<<<dim3(qtiles, slices), THREADS, SMEM_TOTAL, s>>>(tq, tdb, tp);
   }
   CR_CUDA(cudaGetLastError());
-  merge_launch(tp.part_s, tp.part_id, slices * 2, n_queries, k, metric, 0,
-               reinterpret_cast<const __half*>(d_queries), DIM, d_out_dist, d_out_ids, s);
+  if (append)
+    merge_launch(tp.cand_s, nullptr, 0, n_queries, k, metric, 2, reinterpret_cast<const __half*>(d_queries),
+                 DIM, d_out_dist, d_out_ids, s, tp.cand_cnt, cap, tp.cand_r, row_map, row_offset, tp.pub,
+                 n_lists, tp.n_rows);
+  else
+    merge_launch(tp.part_s, tp.part_id, slices * 2, n_queries, k, metric, 0,
+                 reinterpret_cast<const __half*>(d_queries), DIM, d_out_dist, d_out_ids, s);
   uint32_t h_err = 0;
   CR_CUDA(cudaMemcpyAsync(&h_err, tp.err, 4, cudaMemcpyDeviceToHost, s));
   CR_CUDA(cudaStreamSynchronize(s));
@@ -780,6 +899,13 @@ static void run_topk_core(const uint16_t* d_db, const float* norms, uint64_t n_r
     CR_CUDA(cudaMemcpy(c, tp.err, 16, cudaMemcpyDeviceToHost));
     fprintf(stderr, "topk debug: lane flushes %u, warp flush rounds %u, inserts %u\n", c[1], c[2], c[3]);
     h_err = c[0];
+  }
+  if (append && (h_err & kErrOverflow) && !(h_err & ~kErrOverflow)) {
+    // Degenerate score distribution (e.g. massive ties): redo exactly with
+    // per-list merging, which needs no candidate capacity.
+    run_topk_core(d_db, norms, n_rows, pass, row_map, d_queries, n_queries, row_offset, k, metric,
+                  d_out_dist, d_out_ids, s, false);
+    return;
   }
   if (h_err) fail(CR_ERR_DEVICE, "cr_filtered_topk: pipeline wait timed out (code " + std::to_string(h_err) + ")");
 }

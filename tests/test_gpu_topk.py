@@ -125,3 +125,17 @@ def test_topk_no_passing_rows(cr, torch_):
         assert (i.cpu().numpy() == -1).all()
         assert np.isinf(d.cpu().numpy()).all()
     filt.free()
+
+
+def test_topk_all_ties_falls_back_exactly(cr, torch_):
+    """Every row identical: all scores tie, the candidate arrays overflow and
+    the search redoes the batch with per-list merging; ties go to the
+    smallest ids."""
+    n, q, k = 200_000, 40, 10
+    row = np.random.default_rng(0).standard_normal(128).astype(np.float32)
+    row /= np.linalg.norm(row)
+    db = np.tile(row.astype(np.float16), (n, 1))
+    _, qs = make_data(10, q, seed=4)
+    for metric in (0, 1):
+        d, i = cr.filtered_topk(torch_.from_numpy(db).cuda(), torch_.from_numpy(qs).cuda(), k, metric=metric)
+        assert (i.cpu().numpy() == np.arange(k)[None, :]).all()
