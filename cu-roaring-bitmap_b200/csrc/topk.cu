@@ -61,7 +61,8 @@ constexpr uint32_t SMEM_BUF_S = SMEM_DB + STAGES * STAGE_BYTES;
 constexpr uint32_t SMEM_BUF_R = SMEM_BUF_S;
 constexpr uint32_t SMEM_BAR = SMEM_BUF_R;
 constexpr uint32_t SMEM_BOUND = SMEM_BAR + 128;          // float[BM] + done counter
-constexpr uint32_t SMEM_TOTAL = SMEM_BOUND + BM * 4 + 16 + 1024;  // + alignment slack
+constexpr uint32_t SMEM_SV = SMEM_BOUND + BM * 4 + 16;            // float[32][EPI] parked scores
+constexpr uint32_t SMEM_TOTAL = SMEM_SV + 32 * EPI * 4 + 1024;    // + alignment slack
 constexpr uint32_t TMEM_COLS = 512;                     // two 256-column accumulators
 constexpr uint32_t kIdesc = idesc_f16_f32(BM, BN);
 
@@ -85,10 +86,11 @@ struct TopkParams {
   uint32_t jth;          // ceil(k / n_lists)
   const uint32_t* row_map;  // compacted row -> shard row (null: identity)
   uint32_t append;       // 1: survivors go to per-query candidate arrays, no list merges
-  uint32_t cap;          // candidate slots per query (append mode)
-  float* cand_s;         // [Q][cap]
+  uint32_t cap;          // candidate slots per (query, list) (append mode)
+  uint32_t keeper_ns;    // bound keeper refresh period
+  float* cand_s;         // [Q][n_lists][cap]
   uint32_t* cand_r;
-  uint32_t* cand_cnt;    // [Q]
+  uint32_t* cand_cnt;    // [Q][n_lists] entries appended (may exceed cap: overflow)
 };
 
 constexpr uint32_t kErrOverflow = 64u;  // a candidate array filled up (append mode)
@@ -194,6 +196,7 @@ __device__ uint32_t warp_merge_into(const float* bs, const uint32_t* br, uint32_
   return total;
 }
 
+template <bool APPEND>
 __global__ void __launch_bounds__(THREADS, 1)
     k_topk(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tdb,
            TopkParams p)
@@ -215,11 +218,19 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
   float* s_bound = reinterpret_cast<float*>(smem + SMEM_BOUND);
   uint32_t* s_done = reinterpret_cast<uint32_t*>(smem + SMEM_BOUND + BM * 4);
+  float* sv = reinterpret_cast<float*>(smem + SMEM_SV);
 
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t qt = blockIdx.x, slice = blockIdx.y;
   const uint32_t t0 = slice * p.tiles_per_slice;
   const uint32_t t1 = min(p.n_tiles, t0 + p.tiles_per_slice);
+  // Tile schedule. In append mode the first D tiles of the slice run first
+  // in publish-only mode (their best scores feed the shared bound, nothing is
+  // kept), then every tile runs with the bound, those D last.
+  const uint32_t T = t1 - t0;
+  const uint32_t D = APPEND ? min(T, 4u) : 0u;
+  const uint32_t n_it = T + D;
+  auto tile_of = [&](uint32_t it) { return it < T ? t0 + it : t0 + (it - T); };
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -243,8 +254,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_expect_tx(q_full, 2 * KB_BYTES_Q);
       tma_load_2d(&tq, q_full, sQ, 0, int32_t(qt * BM));
       tma_load_2d(&tq, q_full, sQ + KB_BYTES_Q, 64, int32_t(qt * BM));
-      for (uint32_t t = t0; t < t1; ++t) {
-        const uint32_t it = t - t0, s = it % STAGES;
+      for (uint32_t it = 0; it < n_it; ++it) {
+        const uint32_t t = tile_of(it), s = it % STAGES;
         if (!mbar_wait(empty + s, ((it / STAGES) & 1u) ^ 1u, p.err, 1u)) break;
         uint8_t* dst = sDB + s * STAGE_BYTES;
         mbar_expect_tx(full + s, STAGE_BYTES);
@@ -257,8 +268,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       bool ok = mbar_wait(q_full, 0, p.err, 2u);
       const uint32_t aq = smem_addr(sQ);
-      for (uint32_t t = t0; t < t1 && ok; ++t) {
-        const uint32_t it = t - t0, s = it % STAGES, a = it & 1u;
+      for (uint32_t it = 0; it < n_it && ok; ++it) {
+        const uint32_t s = it % STAGES, a = it & 1u;
         if (!mbar_wait(full + s, (it / STAGES) & 1u, p.err, 4u)) break;
         if (!mbar_wait(acc_empty + a, ((it >> 1) & 1u) ^ 1u, p.err, 8u)) break;
         tc_fence_after();
@@ -294,7 +305,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         s_bound[qq] = key_score(min(min(m0, m1), min(m2, m3)));
       }
       if (*reinterpret_cast<volatile uint32_t*>(s_done) >= EPI_WARPS) break;
-      for (int z = 0; z < 20; ++z) __nanosleep(1000);  // the bound moves slowly: refresh every ~20 us
+      __nanosleep(p.keeper_ns);
     }
   } else {
     // ---------------- epilogue: warps 3..10, one thread per (query, half)
@@ -367,8 +378,12 @@ __global__ void __launch_bounds__(THREADS, 1)
     float top1 = -INFINITY, top2 = -INFINITY, top3 = -INFINITY;
     uint32_t published = 0;
     const bool fast_pub = p.jth <= 3;
-    for (uint32_t t = t0; t < t1; ++t) {
-      const uint32_t it = t - t0, a = it & 1u;
+    const uint32_t my_list = slice * 2 + chalf;
+    uint32_t nc = 0;  // candidates this (query, list) appended (append mode)
+    const size_t cand_base = (size_t(qi) * p.n_lists + my_list) * p.cap;
+    for (uint32_t it = 0; it < n_it; ++it) {
+      const uint32_t t = tile_of(it), a = it & 1u;
+      const bool publish_only = it < D;
       if (valid_q) {
         gthr = fmaxf(gthr, key_score(__ldcg(p.shared_thr + qi)));
         // Every list holds >= jth entries >= its published jth best, and
@@ -398,58 +413,49 @@ __global__ void __launch_bounds__(THREADS, 1)
         float mx = -INFINITY;
 #pragma unroll
         for (int j = 0; j < 32; ++j) mx = fmaxf(mx, ((m >> j) & 1u) ? v[j] : -INFINITY);
-        if (__any_sync(0xFFFFFFFFu, valid_q && mx >= bound) && p.debug != 2) {
-          // Candidate rows of this lane, then the union over the warp, so the
-          // rows nobody keeps cost one uniform branch each.
+        const bool want = valid_q && (publish_only || mx >= bound);
+        if (__any_sync(0xFFFFFFFFu, want) && p.debug != 2) {
+          // Slow path, kept compact (instruction-cache friendly): the lane's
+          // candidate rows as a bit mask, its 32 scores parked in shared
+          // memory, then a small loop over the set bits only.
           uint32_t cm = 0;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) cm |= (v[j] >= bound ? 1u : 0u) << j;
-          cm &= valid_q ? m : 0u;
-          const uint32_t any = __reduce_or_sync(0xFFFFFFFFu, cm);
-          if (p.append) {
-            // One reservation per lane per chunk, then rank-ordered stores.
-            const uint32_t n_ins = __popc(cm);
-            uint32_t base = 0;
-            if (n_ins) base = atomicAdd(p.cand_cnt + qi, n_ins);
-            const bool fits = base + n_ins <= p.cap;
-            if (n_ins && !fits) atomicOr(p.err, kErrOverflow);
-            const size_t qb = size_t(qi) * p.cap;
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              if (!((any >> j) & 1u)) continue;
-              if ((cm >> j) & 1u) {
-                const float x = v[j];
-                if (fits) {
-                  const uint32_t at = base + __popc(cm & ((1u << j) - 1u));
-                  p.cand_s[qb + at] = x;
-                  p.cand_r[qb + at] = r0 + j;
-                }
-                if (x > top1) { top3 = top2; top2 = top1; top1 = x; }
-                else if (x > top2) { top3 = top2; top2 = x; }
-                else if (x > top3) { top3 = x; }
-              }
-            }
-            continue;
-          }
-#pragma unroll
           for (int j = 0; j < 32; ++j) {
-            if (!((any >> j) & 1u)) continue;
+            cm |= (v[j] >= bound ? 1u : 0u) << j;
+            sv[j * EPI + e_local] = v[j];
+          }
+          cm = want ? (publish_only ? m : (cm & m)) : 0u;
+          if (APPEND && !publish_only && p.debug == 3) {
+            if (cm) atomicAdd(p.err + 3, __popc(cm));
+            if (lane == 0) atomicAdd(p.err + 2, 1u);
+          }
+#pragma unroll 1
+          for (uint32_t x = cm; x; x &= x - 1) {
+            const uint32_t j = __ffs(x) - 1;
+            const float val = sv[j * EPI + e_local];
             const uint32_t r = r0 + j;
-            if (((cm >> j) & 1u) && v[j] >= gthr && better(v[j], r, thr_s, thr_r)) {
-              if (p.debug == 3) atomicAdd(p.err + 3, 1u);
-              if (fast_pub) {
-                const float x = v[j];
-                if (x > top1) { top3 = top2; top2 = top1; top1 = x; }
-                else if (x > top2) { top3 = top2; top2 = x; }
-                else if (x > top3) { top3 = x; }
+            if (APPEND) {
+              if (!publish_only) {
+                if (nc < p.cap) {
+                  p.cand_s[cand_base + nc] = val;
+                  p.cand_r[cand_base + nc] = r;
+                }
+                ++nc;
               }
-              mybuf_s[nb] = v[j];
+            } else {
+              if (!(val >= gthr && better(val, r, thr_s, thr_r))) continue;
+              mybuf_s[nb] = val;
               mybuf_r[nb] = r;
               ++nb;
             }
+            if (fast_pub && val > top3) {
+              if (val > top1) { top3 = top2; top2 = top1; top1 = val; }
+              else if (val > top2) { top3 = top2; top2 = val; }
+              else { top3 = val; }
+            }
           }
         }
-        flush(32);  // at most 31 + 32 entries are ever buffered
+        if (!APPEND) flush(32);  // at most 31 + 32 entries are ever buffered
       }
       tc_fence_before();
       __syncwarp();
@@ -463,10 +469,14 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
     }
-    flush(1);
+    if (!APPEND) flush(1);
+    if (APPEND && valid_q) {
+      p.cand_cnt[size_t(qi) * p.n_lists + my_list] = nc;
+      if (nc > p.cap) atomicOr(p.err, kErrOverflow);
+    }
     if (lane == 0) atomicAdd(s_done, 1u);
     // Coalesced copy of each lane's final list into this slice's output.
-    for (uint32_t f = 0; f < (p.append ? 0u : 32u); ++f) {
+    for (uint32_t f = 0; f < (APPEND ? 0u : 32u); ++f) {
       const uint32_t fq = qt * BM + quarter * 32 + f;
       if (fq >= p.n_queries) break;
       const uint32_t f_cnt = __shfl_sync(0xFFFFFFFFu, cnt, f);
@@ -559,9 +569,17 @@ __global__ void __launch_bounds__(MERGE_THREADS) k_merge(const float* part_s, co
     __syncthreads();
     bound = key_score(s_min);
   }
-  // An overflowed candidate array has unwritten slots; that pass is redone
-  // by the caller, so the query is skipped here.
-  const uint64_t total = kind == 2 ? (cand_cnt[q] > cap ? 0u : cand_cnt[q]) : uint64_t(parts) * k;
+  // kind 2: n_lists regions of `cap` slots per query. An overflowed region
+  // has unwritten slots; that pass is redone by the caller, so skip it here.
+  __shared__ uint32_t s_over;
+  if (kind == 2) {
+    if (threadIdx.x == 0) s_over = 0;
+    __syncthreads();
+    for (uint32_t l = threadIdx.x; l < n_lists; l += MERGE_THREADS)
+      if (cand_cnt[size_t(q) * n_lists + l] > cap) s_over = 1;
+    __syncthreads();
+  }
+  const uint64_t total = kind == 2 ? (s_over ? 0u : uint64_t(n_lists) * cap) : uint64_t(parts) * k;
   auto load = [&](uint64_t c, uint32_t slot) {
     float v = -INFINITY;
     int64_t i = -1;
@@ -604,7 +622,9 @@ __global__ void __launch_bounds__(MERGE_THREADS) k_merge(const float* part_s, co
       for (uint32_t j = threadIdx.x; j < B; j += MERGE_THREADS) {
         const uint64_t c = c0 + j;
         if (c >= total) break;
-        const size_t g = size_t(q) * cap + c;
+        const uint32_t l = static_cast<uint32_t>(c / cap), e = static_cast<uint32_t>(c % cap);
+        if (e >= cand_cnt[size_t(q) * n_lists + l]) continue;
+        const size_t g = size_t(q) * n_lists * cap + c;
         const float x = part_s[g];
         const uint32_t r = cand_r[g];
         if (x >= bound && r < n_rows) {
@@ -822,7 +842,8 @@ static void run_topk_core(const uint16_t* d_db, const float* norms, uint64_t n_r
 {
   static std::once_flag once;
   std::call_once(once, [] {
-    cudaFuncSetAttribute(k_topk, cudaFuncAttributeMaxDynamicSharedMemorySize, int(SMEM_TOTAL));
+    cudaFuncSetAttribute(k_topk<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(SMEM_TOTAL));
+    cudaFuncSetAttribute(k_topk<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(SMEM_TOTAL));
   });
   const uint32_t n_tiles = div_up(n_rows, BN);
   const uint32_t qtiles = div_up(n_queries, BM);
@@ -839,9 +860,10 @@ static void run_topk_core(const uint16_t* d_db, const float* norms, uint64_t n_r
   // Append mode needs the register-tracked list bounds (jth <= 3); its
   // candidate arrays hold up to `cap` survivors per query.
   const bool append = allow_append && jth <= 3;
-  const uint32_t cap = append ? std::max<uint32_t>(32768u, 128u * k) : 0u;
-  const size_t cand_b = append ? size_t(n_queries) * cap * 4 : 0;
-  Scratch scr(list_b * 2 + cbuf_b * 2 + part_b * 12 + pub_b + cand_b * 2 + size_t(n_queries) * 8 + 64 + 512, s);
+  const uint32_t cap = append ? std::max<uint32_t>(256u, div_up(std::max<uint32_t>(32768u, 128u * k), n_lists)) : 0u;
+  const size_t cand_b = append ? size_t(n_queries) * n_lists * cap * 4 : 0;
+  Scratch scr(list_b * 2 + cbuf_b * 2 + part_b * 12 + pub_b + cand_b * 2 + size_t(n_queries) * n_lists * 4 +
+                  size_t(n_queries) * 8 + 64 + 512, s);
   char* p = scr.as<char>();
   TopkParams tp{};
   tp.n_rows = static_cast<uint32_t>(n_rows);
@@ -867,8 +889,8 @@ static void run_topk_core(const uint16_t* d_db, const float* norms, uint64_t n_r
   if (append) {
     tp.cand_s = reinterpret_cast<float*>(p); p += cand_b;
     tp.cand_r = reinterpret_cast<uint32_t*>(p); p += cand_b;
-    tp.cand_cnt = reinterpret_cast<uint32_t*>(p); p += size_t(n_queries) * 4;
-    CR_CUDA(cudaMemsetAsync(tp.cand_cnt, 0, size_t(n_queries) * 4, s));
+    tp.cand_cnt = reinterpret_cast<uint32_t*>(p); p += size_t(n_queries) * n_lists * 4;
+    CR_CUDA(cudaMemsetAsync(tp.cand_cnt, 0, size_t(n_queries) * n_lists * 4, s));
   }
   tp.part_id = reinterpret_cast<int64_t*>(p); p += part_b * 8;
   tp.part_s = reinterpret_cast<float*>(p); p += part_b * 4;
@@ -876,12 +898,15 @@ static void run_topk_core(const uint16_t* d_db, const float* norms, uint64_t n_r
   tp.err = reinterpret_cast<uint32_t*>(p);
   tp.shared_thr = tp.err + 4;
   if (const char* dbg = getenv("CR_TOPK_DEBUG")) tp.debug = uint32_t(atoi(dbg));
+  tp.keeper_ns = 2000;
+  if (const char* kn = getenv("CR_TOPK_KEEPER_NS")) tp.keeper_ns = uint32_t(atoi(kn));
   CR_CUDA(cudaMemsetAsync(tp.err, 0, 16 + size_t(n_queries) * 4, s));
   const CUtensorMap tq = make_map(d_queries, n_queries, BM);
   const CUtensorMap tdb = make_map(d_db, n_rows, BN);
   {
     ProfileScope prof(CR_KERNEL_TOPK, s);
-    k_topk<<<dim3(qtiles, slices), THREADS, SMEM_TOTAL, s>>>(tq, tdb, tp);
+    if (append) k_topk<true><<<dim3(qtiles, slices), THREADS, SMEM_TOTAL, s>>>(tq, tdb, tp);
+    else k_topk<false><<<dim3(qtiles, slices), THREADS, SMEM_TOTAL, s>>>(tq, tdb, tp);
   }
   CR_CUDA(cudaGetLastError());
   if (append)
@@ -897,7 +922,7 @@ static void run_topk_core(const uint16_t* d_db, const float* norms, uint64_t n_r
   if (tp.debug == 3) {
     uint32_t c[4];
     CR_CUDA(cudaMemcpy(c, tp.err, 16, cudaMemcpyDeviceToHost));
-    fprintf(stderr, "topk debug: lane flushes %u, warp flush rounds %u, inserts %u\n", c[1], c[2], c[3]);
+    fprintf(stderr, "topk debug: lane flushes %u, warp slow paths / flush rounds %u, inserts %u\n", c[1], c[2], c[3]);
     h_err = c[0];
   }
   if (append && (h_err & kErrOverflow) && !(h_err & ~kErrOverflow)) {
