@@ -508,11 +508,12 @@ __device__ __forceinline__ bool better64(float as, int64_t ai, float bs, int64_t
   return as > bs || (as == bs && ua < ub);
 }
 
-__device__ void bitonic_sort(float* s, int64_t* id)
+// Sorts the first n slots (n a power of two, 2 <= n <= MERGE_N), best first.
+__device__ void bitonic_sort(float* s, int64_t* id, uint32_t n = MERGE_N)
 {
-  for (uint32_t size = 2; size <= MERGE_N; size <<= 1) {
+  for (uint32_t size = 2; size <= n; size <<= 1) {
     for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
-      for (uint32_t pr = threadIdx.x; pr < MERGE_N / 2; pr += MERGE_THREADS) {
+      for (uint32_t pr = threadIdx.x; pr < n / 2; pr += MERGE_THREADS) {
         const uint32_t i = (pr / stride) * 2 * stride + (pr % stride), j = i + stride;
         const bool first_better = better64(s[i], id[i], s[j], id[j]);
         const bool want_first_better = (i & size) == 0;
@@ -611,31 +612,34 @@ __global__ void __launch_bounds__(MERGE_THREADS) k_merge(const float* part_s, co
     if (threadIdx.x == 0) s_fill = 0;
     __syncthreads();
     constexpr uint32_t B = 2 * MERGE_THREADS;
-    for (uint64_t c0 = 0; c0 < total; c0 += B) {
-      if (s_fill + B > MERGE_N - k) {
-        bitonic_sort(s, id);
-        for (uint32_t i = k + threadIdx.x; i < MERGE_N; i += MERGE_THREADS) { s[i] = -INFINITY; id[i] = -1; }
-        __syncthreads();
-        if (threadIdx.x == 0) s_fill = 0;
-        __syncthreads();
-      }
-      for (uint32_t j = threadIdx.x; j < B; j += MERGE_THREADS) {
-        const uint64_t c = c0 + j;
-        if (c >= total) break;
-        const uint32_t l = static_cast<uint32_t>(c / cap), e = static_cast<uint32_t>(c % cap);
-        if (e >= cand_cnt[size_t(q) * n_lists + l]) continue;
-        const size_t g = size_t(q) * n_lists * cap + c;
-        const float x = part_s[g];
-        const uint32_t r = cand_r[g];
-        if (x >= bound && r < n_rows) {
-          const uint32_t slot = k + atomicAdd(&s_fill, 1u);
-          s[slot] = x;
-          id[slot] = int64_t(row_map ? __ldg(row_map + r) : r) + int64_t(row_offset);
+    // Walk only the filled part of each list's region.
+    for (uint32_t l = 0; l < (total ? n_lists : 0u); ++l) {
+      const uint32_t cnt = cand_cnt[size_t(q) * n_lists + l];
+      for (uint32_t e0 = 0; e0 < cnt; e0 += B) {
+        if (s_fill + B > MERGE_N - k) {
+          bitonic_sort(s, id);
+          for (uint32_t i = k + threadIdx.x; i < MERGE_N; i += MERGE_THREADS) { s[i] = -INFINITY; id[i] = -1; }
+          __syncthreads();
+          if (threadIdx.x == 0) s_fill = 0;
+          __syncthreads();
         }
+        for (uint32_t e = e0 + threadIdx.x; e < min(cnt, e0 + B); e += MERGE_THREADS) {
+          const size_t g = (size_t(q) * n_lists + l) * cap + e;
+          const float x = part_s[g];
+          const uint32_t r = cand_r[g];
+          if (x >= bound && r < n_rows) {
+            const uint32_t slot = k + atomicAdd(&s_fill, 1u);
+            s[slot] = x;
+            id[slot] = int64_t(row_map ? __ldg(row_map + r) : r) + int64_t(row_offset);
+          }
+        }
+        __syncthreads();
       }
-      __syncthreads();
     }
-    bitonic_sort(s, id);
+    // Sort just the occupied prefix (rounded up to a power of two).
+    uint32_t n_sort = 2;
+    while (n_sort < k + s_fill) n_sort <<= 1;
+    bitonic_sort(s, id, min(n_sort, MERGE_N));
   } else {
     uint64_t pos = 0;
     for (uint32_t i = threadIdx.x; i < MERGE_N; i += MERGE_THREADS) load(pos + i, i);
