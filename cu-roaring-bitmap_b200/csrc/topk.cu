@@ -500,6 +500,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 // ------------------------------------------------------------------ merge
 constexpr uint32_t MERGE_N = 4096;
 constexpr uint32_t MERGE_THREADS = 512;
+constexpr uint32_t kMaxListsMerge = 511;  // partial lists per query in append mode
 
 __device__ __forceinline__ bool better64(float as, int64_t ai, float bs, int64_t bi)
 {
@@ -612,29 +613,44 @@ __global__ void __launch_bounds__(MERGE_THREADS) k_merge(const float* part_s, co
     if (threadIdx.x == 0) s_fill = 0;
     __syncthreads();
     constexpr uint32_t B = 2 * MERGE_THREADS;
-    // Walk only the filled part of each list's region.
-    for (uint32_t l = 0; l < (total ? n_lists : 0u); ++l) {
-      const uint32_t cnt = cand_cnt[size_t(q) * n_lists + l];
-      for (uint32_t e0 = 0; e0 < cnt; e0 += B) {
-        if (s_fill + B > MERGE_N - k) {
-          bitonic_sort(s, id);
-          for (uint32_t i = k + threadIdx.x; i < MERGE_N; i += MERGE_THREADS) { s[i] = -INFINITY; id[i] = -1; }
-          __syncthreads();
-          if (threadIdx.x == 0) s_fill = 0;
-          __syncthreads();
-        }
-        for (uint32_t e = e0 + threadIdx.x; e < min(cnt, e0 + B); e += MERGE_THREADS) {
-          const size_t g = (size_t(q) * n_lists + l) * cap + e;
-          const float x = part_s[g];
-          const uint32_t r = cand_r[g];
-          if (x >= bound && r < n_rows) {
-            const uint32_t slot = k + atomicAdd(&s_fill, 1u);
-            s[slot] = x;
-            id[slot] = int64_t(row_map ? __ldg(row_map + r) : r) + int64_t(row_offset);
-          }
-        }
+    // One pass over the filled part of every list region: prefix of the
+    // per-list counts in shared memory, flattened index -> (list, entry).
+    __shared__ uint32_t s_pre[kMaxListsMerge + 1];
+    const uint32_t nl = total ? n_lists : 0u;
+    if (threadIdx.x == 0) {
+      uint32_t acc = 0;
+      for (uint32_t l = 0; l < nl; ++l) {
+        s_pre[l] = acc;
+        acc += cand_cnt[size_t(q) * n_lists + l];
+      }
+      s_pre[nl] = acc;
+    }
+    __syncthreads();
+    const uint32_t n_valid = s_pre[nl];
+    for (uint32_t c0 = 0; c0 < n_valid; c0 += B) {
+      if (s_fill + B > MERGE_N - k) {
+        bitonic_sort(s, id);
+        for (uint32_t i = k + threadIdx.x; i < MERGE_N; i += MERGE_THREADS) { s[i] = -INFINITY; id[i] = -1; }
+        __syncthreads();
+        if (threadIdx.x == 0) s_fill = 0;
         __syncthreads();
       }
+      for (uint32_t c = c0 + threadIdx.x; c < min(n_valid, c0 + B); c += MERGE_THREADS) {
+        uint32_t lo = 0, hi = nl;  // last list whose prefix <= c
+        while (hi - lo > 1) {
+          const uint32_t mid = (lo + hi) >> 1;
+          if (s_pre[mid] <= c) lo = mid; else hi = mid;
+        }
+        const size_t g = (size_t(q) * n_lists + lo) * cap + (c - s_pre[lo]);
+        const float x = part_s[g];
+        const uint32_t r = cand_r[g];
+        if (x >= bound && r < n_rows) {
+          const uint32_t slot = k + atomicAdd(&s_fill, 1u);
+          s[slot] = x;
+          id[slot] = int64_t(row_map ? __ldg(row_map + r) : r) + int64_t(row_offset);
+        }
+      }
+      __syncthreads();
     }
     // Sort just the occupied prefix (rounded up to a power of two).
     uint32_t n_sort = 2;
@@ -863,7 +879,7 @@ static void run_topk_core(const uint16_t* d_db, const float* norms, uint64_t n_r
   const uint32_t jth = (k + n_lists - 1) / n_lists;
   // Append mode needs the register-tracked list bounds (jth <= 3); its
   // candidate arrays hold up to `cap` survivors per query.
-  const bool append = allow_append && jth <= 3;
+  const bool append = allow_append && jth <= 3 && n_lists <= kMaxListsMerge;
   const uint32_t cap = append ? std::max<uint32_t>(256u, div_up(std::max<uint32_t>(32768u, 128u * k), n_lists)) : 0u;
   const size_t cand_b = append ? size_t(n_queries) * n_lists * cap * 4 : 0;
   Scratch scr(list_b * 2 + cbuf_b * 2 + part_b * 12 + pub_b + cand_b * 2 + size_t(n_queries) * n_lists * 4 +
