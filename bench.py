@@ -106,54 +106,72 @@ def gen_queries(torch, device):
 # -------------------------------------------------------------- clocks
 
 class ClockSampler:
-    """nvidia-smi samples of this GPU during the timed region."""
+    """SM clock and throttle reasons of this GPU, polled through NVML every
+    ~2 ms on a background thread during the timed region (a timed region of a
+    few milliseconds still gets samples; nvidia-smi's loop is too coarse)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clocks-event reason bits
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
 
-    def __init__(self, gpu_index: int):
-        self.idx = gpu_index
-        self.proc = None
+    def __init__(self, torch_device_index: int):
+        self.idx = torch_device_index
+        self.samples = []
+        self.max_mhz = None
+        self._stop = False
+        self._thread = None
+        self._ok = False
 
     def __enter__(self):
+        import threading
+
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-i", str(self.idx), "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
-                text=True)
+            import pynvml
+
+            pynvml.nvmlInit()
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+            phys = self.idx
+            if vis:
+                try:
+                    phys = int(vis.split(",")[self.idx])
+                except ValueError:
+                    phys = self.idx
+            h = pynvml.nvmlDeviceGetHandleByIndex(phys)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+
+            def poll():
+                while not self._stop:
+                    try:
+                        mhz = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                        rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                        self.samples.append((mhz, rs))
+                    except Exception:
+                        pass
+                    time.sleep(0.002)
+
+            self._ok = True
+            self._thread = threading.Thread(target=poll, daemon=True)
+            self._thread.start()
         except Exception:
-            self.proc = None
+            self._ok = False
         return self
 
     def __exit__(self, *exc):
-        if self.proc:
-            self.proc.terminate()
-            try:
-                self.out = self.proc.communicate(timeout=5)[0]
-            except Exception:
-                self.proc.kill()
-                self.out = ""
+        self._stop = True
+        if self._thread:
+            self._thread.join(timeout=2)
 
     def summary(self):
-        if not self.proc:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in getattr(self, "out", "").strip().split("\n"):
-            f = [x.strip() for x in line.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(n)
-        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        if not self._ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"], "samples": 0}
+        reasons = set()
+        for _, rs in self.samples:
+            for bit, name in self.REASONS.items():
+                if rs & bit:
+                    reasons.add(name)
+        mhz = [m for m, _ in self.samples]
+        return {"sm_mhz": float(np.median(mhz)) if mhz else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(mhz), "source": "nvml, 2 ms polling"}
 
 
 # ----------------------------------------------------------- CPU sides
@@ -321,7 +339,7 @@ def main():
     pk, pk_kind = peaks()
 
     n_rows = args.rows
-    lo, hi = n_rows * rank // world, n_rows * (rank + 1) // world
+    lo, hi = cr.shard_range(n_rows, rank, world)
     db = gen_rows(torch, lo, hi, dev)
     tset = choose_tag_set(torch, dev, PASS_TARGET)
     mask = torch.isin(gen_tags(torch, lo, hi, dev), tset).any(dim=1)
@@ -356,14 +374,7 @@ def main():
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     kernel_ms = []
-    gpu_index = local
-    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
-    if vis:
-        try:
-            gpu_index = int(vis.split(",")[local])
-        except ValueError:
-            pass
-    with ClockSampler(gpu_index) as clocks:
+    with ClockSampler(local) as clocks:
         ev0.record(stream)
         for _ in range(args.steps):
             step(queries)

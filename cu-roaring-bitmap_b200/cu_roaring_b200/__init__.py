@@ -392,3 +392,12 @@ def profile_last_ms(kernel: int) -> float:
     v = C.c_float()
     _check(_lib.cr_profile_last_ms(kernel, C.byref(v)), "profile_last_ms")
     return v.value
+
+
+# ------------------------------------------------------------- sharding
+
+def shard_range(n_rows: int, rank: int, world: int) -> tuple[int, int]:
+    """Contiguous row range [lo, hi) of `rank` when n_rows are split over
+    `world` ranks (the filtered top-k shards the database this way; row IDs
+    stay global via row_offset = lo)."""
+    return n_rows * rank // world, n_rows * (rank + 1) // world
