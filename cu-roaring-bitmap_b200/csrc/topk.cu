@@ -409,10 +409,22 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int j = 0; j < 32; ++j)  // rows past the mask (and n_rows) are never read
             v[j] = ((m >> j) & 1u) ? 2.f * v[j] - __ldg(p.norms + r0 + j) : -INFINITY;
         }
-        // Fast path: the best passing score of the chunk against the bound.
-        float mx = -INFINITY;
+        // Fast path: the best passing score of the chunk against the bound
+        // (a 5-level max tree, not a 32-long dependency chain).
+        float t16[16];
+        if (m == 0xFFFFFFFFu) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) mx = fmaxf(mx, ((m >> j) & 1u) ? v[j] : -INFINITY);
+          for (int j = 0; j < 16; ++j) t16[j] = fmaxf(v[j], v[j + 16]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            t16[j] = fmaxf(((m >> j) & 1u) ? v[j] : -INFINITY, ((m >> (j + 16)) & 1u) ? v[j + 16] : -INFINITY);
+        }
+#pragma unroll
+        for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+          for (int j = 0; j < w; ++j) t16[j] = fmaxf(t16[j], t16[j + w]);
+        const float mx = t16[0];
         const bool want = valid_q && (publish_only || mx >= bound);
         if (__any_sync(0xFFFFFFFFu, want) && p.debug != 2) {
           // Slow path, kept compact (instruction-cache friendly): the lane's
