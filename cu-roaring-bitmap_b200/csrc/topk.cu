@@ -430,12 +430,14 @@ __global__ void __launch_bounds__(THREADS, 1)
           // Slow path, kept compact (instruction-cache friendly): the lane's
           // candidate rows as a bit mask, its 32 scores parked in shared
           // memory, then a small loop over the set bits only.
-          uint32_t cm = 0;
+          uint32_t c8[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};  // 8 independent OR chains
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
-            cm |= (v[j] >= bound ? 1u : 0u) << j;
+            c8[j & 7] |= (v[j] >= bound ? 1u : 0u) << j;
             sv[j * EPI + e_local] = v[j];
           }
+          const uint32_t cm0 = (c8[0] | c8[1]) | (c8[2] | c8[3]);
+          uint32_t cm = cm0 | ((c8[4] | c8[5]) | (c8[6] | c8[7]));
           cm = want ? (publish_only ? m : (cm & m)) : 0u;
           if (APPEND && !publish_only && p.debug == 3) {
             if (cm) atomicAdd(p.err + 3, __popc(cm));
@@ -695,16 +697,71 @@ __global__ void __launch_bounds__(MERGE_THREADS) k_merge(const float* part_s, co
 
 // Shard-local pass bitset: bit i of word w = filter.contains(row_offset + 32w + i).
 __global__ void k_pass_bits(cu_roaring::GpuRoaringView v, uint64_t row_offset, uint64_t n_rows,
-                            uint32_t* out, uint64_t n_words)
+                            uint32_t* out, uint64_t n_words, uint64_t universe)
 {
   const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
   for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n_words * 32; i += stride) {
     const uint64_t id = row_offset + i;
-    const bool ok = i < n_rows && id <= 0xFFFFFFFFull;
+    const bool ok = i < n_rows && id < universe;  // IDs past the universe are never members
     const bool hit = cu_roaring::warp_contains(v, ok ? uint32_t(id) : 0u) && ok;
     const uint32_t bits = __ballot_sync(0xFFFFFFFFu, hit);
     if ((threadIdx.x & 31) == 0) out[i >> 5] = bits;
   }
+}
+
+// Same, one thread per output word when row_offset is a multiple of 32 (the
+// 32 IDs of a word then share one container): one key lookup per word; a
+// BITMAP container gives the word directly, ARRAY and RUN containers are
+// searched for the word's 32-ID window.
+__global__ void k_pass_words(DevBitmap b, uint64_t row_offset, uint64_t n_rows, uint32_t* out,
+                             uint64_t n_words)
+{
+  const uint64_t w = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (w >= n_words) return;
+  const uint64_t id0 = row_offset + w * 32;
+  uint32_t bits = 0;
+  if (id0 <= 0xFFFFFFFFull) {
+    const uint32_t key = uint32_t(id0 >> 16), low0 = uint32_t(id0 & 0xFFFFu);
+    const ContainerRef c = dev_container(b, dev_lookup(b, key));
+    if (c.idx >= 0) {
+      if (c.type == kBitmap) {
+        bits = __ldg(reinterpret_cast<const uint32_t*>(b.bitmap + (c.off >> 3)) + (low0 >> 5));
+      } else if (c.type == kArray) {
+        const uint16_t* a = b.array + (c.off >> 1);
+        uint32_t lo = 0, hi = c.card;  // first element >= low0
+        while (lo < hi) {
+          const uint32_t mid = (lo + hi) >> 1;
+          if (__ldg(a + mid) < low0) lo = mid + 1; else hi = mid;
+        }
+        for (uint32_t i = lo; i < c.card; ++i) {
+          const uint32_t v = __ldg(a + i);
+          if (v >= low0 + 32) break;
+          bits |= 1u << (v - low0);
+        }
+      } else {
+        const uint16_t* r = b.run + (c.off >> 1);
+        uint32_t lo = 0, hi = c.card;  // first run ending at or after low0
+        while (lo < hi) {
+          const uint32_t mid = (lo + hi) >> 1;
+          if (uint32_t(__ldg(r + 2 * mid)) + __ldg(r + 2 * mid + 1) < low0) lo = mid + 1; else hi = mid;
+        }
+        for (uint32_t i = lo; i < c.card; ++i) {
+          const uint32_t st = __ldg(r + 2 * i), en = st + __ldg(r + 2 * i + 1);
+          if (st >= low0 + 32) break;
+          const uint32_t a0 = max(st, low0) - low0, a1 = min(en, low0 + 31) - low0;
+          bits |= (a1 == 31 ? 0xFFFFFFFFu : ((1u << (a1 + 1)) - 1u)) & ~((1u << a0) - 1u);
+        }
+      }
+    }
+  }
+  if (b.negated) bits = ~bits;
+  // IDs at or past the universe are never members; rows past n_rows are cleared.
+  const uint64_t U = b.universe;
+  for (uint32_t j = 0; j < 32; ++j) {
+    const uint64_t id = id0 + j;
+    if (w * 32 + j >= n_rows || id >= U) bits &= ~(1u << j);
+  }
+  out[w] = bits;
 }
 
 // Squared norms, 16 lanes per 128-dim row (16 bytes each).
@@ -1005,12 +1062,16 @@ extern "C" int cr_filtered_topk(const uint16_t* d_db, const float* d_db_norms, u
   uint32_t* pass = pass_scr.as<uint32_t>();
   uint32_t* d_total = pass + pass_words;
   uint32_t* tiles = d_total + 4;
-  {
+  Scratch kidx_holder;
+  if (row_offset % 32 == 0) {
+    const DevBitmap b = make_dev(filter, kidx_holder, s);
+    k_pass_words<<<div_up(pass_words, 256), 256, 0, s>>>(b, row_offset, n_rows, pass, pass_words);
+  } else {
     const cu_roaring::GpuRoaringView v =
         cu_roaring::make_view(*reinterpret_cast<const cu_roaring::GpuRoaring*>(filter));
     const uint64_t threads = pass_words * 32;
     const int grid = static_cast<int>(std::min<uint64_t>(div_up(threads, 256), uint64_t(sm_count()) * 16));
-    k_pass_bits<<<grid, 256, 0, s>>>(v, row_offset, n_rows, pass, pass_words);
+    k_pass_bits<<<grid, 256, 0, s>>>(v, row_offset, n_rows, pass, pass_words, filter->universe_size);
   }
   k_pass_tile_sums<<<n_wtiles, kWordTile, 0, s>>>(pass, pass_words, tiles);
   CR_CUDA(cudaGetLastError());

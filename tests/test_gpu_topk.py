@@ -139,3 +139,37 @@ def test_topk_all_ties_falls_back_exactly(cr, torch_):
     for metric in (0, 1):
         d, i = cr.filtered_topk(torch_.from_numpy(db).cuda(), torch_.from_numpy(qs).cuda(), k, metric=metric)
         assert (i.cpu().numpy() == np.arange(k)[None, :]).all()
+
+
+@pytest.mark.parametrize("kind", ["runs", "negated", "array_sparse", "offset_not_32"])
+def test_topk_filter_container_kinds(cr, oracle, torch_, kind):
+    """Filters made of RUN containers, a negated (complement-stored) filter,
+    sparse ARRAY containers, and a shard offset that is not a multiple of 32
+    (per-row membership path)."""
+    n, q, k = 140_000, 50, 20
+    db, qs = make_data(n, q, seed=11)
+    rng = np.random.default_rng(8)
+    if kind == "runs":
+        ids = np.concatenate([np.arange(s, s + 3000) for s in range(0, n - 3000, 9000)]).astype(np.uint32)
+    elif kind == "negated":
+        ids = np.flatnonzero(rng.random(n) < 0.9).astype(np.uint32)
+    else:
+        ids = np.flatnonzero(rng.random(n) < 0.003).astype(np.uint32)
+    lo = 0 if kind != "offset_not_32" else 1000 + 7
+    filt = cr.upload_from_ids(ids, n, bitmap_threshold=4096)
+    if kind == "runs":
+        assert filt.raw.n_run_containers > 0
+    if kind == "negated":
+        assert filt.raw.negated
+    words = np.zeros((n + 31) // 32, dtype=np.uint32)
+    np.bitwise_or.at(words, ids // 32, (1 << (ids % 32)).astype(np.uint32))
+    shard = db[lo:]
+    sub = np.zeros(((n - lo) + 31) // 32, dtype=np.uint32)
+    sel = ids[ids >= lo] - lo
+    np.bitwise_or.at(sub, sel // 32, (1 << (sel % 32)).astype(np.uint32))
+    d_ref, i_ref = oracle.topk(shard, qs, k, 0, sub)
+    i_ref = np.where(i_ref >= 0, i_ref + lo, -1)
+    d, i = cr.filtered_topk(torch_.from_numpy(np.ascontiguousarray(shard)).cuda(), torch_.from_numpy(qs).cuda(),
+                            k, metric=0, filter=filt, row_offset=lo)
+    check_topk(d.cpu().numpy(), i.cpu().numpy(), d_ref, i_ref, 0)
+    filt.free()
