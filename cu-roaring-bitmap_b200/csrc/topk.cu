@@ -47,7 +47,9 @@ constexpr uint32_t BM = 128;       // queries per CTA (UMMA M, TMEM lanes)
 constexpr uint32_t BN = 256;       // database rows per tile (UMMA N)
 constexpr uint32_t DIM = 128;      // K
 constexpr uint32_t STAGES = 2;
-constexpr uint32_t EPI_WARPS = 8;  // two per TMEM lane quarter, each on half the columns
+constexpr uint32_t EPI_WARPS = 16;  // four per TMEM lane quarter, each on a quarter of the columns
+constexpr uint32_t EPI_PARTS = EPI_WARPS / 4;          // column parts (partial lists per slice)
+constexpr uint32_t PART_CHUNKS = (BN / 32) / EPI_PARTS; // 32-row chunks per part
 constexpr uint32_t EPI = EPI_WARPS * 32;
 constexpr uint32_t BUF = 64;       // candidate buffer entries per (query, half); flushed at >= 32
 constexpr uint32_t THREADS = 96 + EPI;  // producer, MMA, bound keeper, 8 epilogue warps
@@ -310,15 +312,15 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else {
     // ---------------- epilogue: warps 3..10, one thread per (query, half)
     const uint32_t quarter = warp & 3u;               // TMEM lane quarter this warp may access
-    const uint32_t chalf = (warp - EPI_WARP0) >> 2;   // which 128 columns (rows of the tile)
+    const uint32_t chalf = (warp - EPI_WARP0) >> 2;   // which column part (rows of the tile)
     const uint32_t t_local = quarter * 32 + lane;     // query row inside the tile
     const uint32_t e_local = chalf * BM + t_local;    // this thread's (half, query) slot
     const uint32_t qi = qt * BM + t_local;
     const bool valid_q = qi < p.n_queries;
     const size_t cta = size_t(slice) * gridDim.x + qt;
     // This warp's 32 lists: [lane][half][k], contiguous per query.
-    float* Lw_s = p.list_s + ((cta * 2 + chalf) * BM + quarter * 32) * 2 * p.k;
-    uint32_t* Lw_r = p.list_r + ((cta * 2 + chalf) * BM + quarter * 32) * 2 * p.k;
+    float* Lw_s = p.list_s + ((cta * EPI_PARTS + chalf) * BM + quarter * 32) * 2 * p.k;
+    uint32_t* Lw_r = p.list_r + ((cta * EPI_PARTS + chalf) * BM + quarter * 32) * 2 * p.k;
     float* mybuf_s = buf_s + e_local * BUF;
     uint32_t* mybuf_r = buf_r + e_local * BUF;
     uint32_t half = 0, cnt = 0, nb = 0, thr_r = 0xFFFFFFFFu;
@@ -359,7 +361,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         jth.s = __shfl_sync(0xFFFFFFFFu, jth.s, (p.jth - 1) & 31u);
         if (lane == f) {
           if (!(p.jth <= 3) && f_cnt >= p.jth)
-            p.pub[size_t(slice * 2 + chalf) * p.n_queries + qi] = score_key(jth.s);
+            p.pub[size_t(slice * EPI_PARTS + chalf) * p.n_queries + qi] = score_key(jth.s);
           nb = 0;
           cnt = f_cnt;
           half = f_half;
@@ -378,7 +380,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     float top1 = -INFINITY, top2 = -INFINITY, top3 = -INFINITY;
     uint32_t published = 0;
     const bool fast_pub = p.jth <= 3;
-    const uint32_t my_list = slice * 2 + chalf;
+    const uint32_t my_list = slice * EPI_PARTS + chalf;
     uint32_t nc = 0;  // candidates this (query, list) appended (append mode)
     const size_t cand_base = (size_t(qi) * p.n_lists + my_list) * p.cap;
     for (uint32_t it = 0; it < n_it; ++it) {
@@ -395,7 +397,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t row0 = t * BN;
       const float bound = fmaxf(gthr, thr_s);
 #pragma unroll 1
-      for (uint32_t c = chalf * 4; c < (p.debug == 1 ? 0u : chalf * 4 + 4); ++c) {
+      for (uint32_t c = chalf * PART_CHUNKS; c < (p.debug == 1 ? 0u : (chalf + 1) * PART_CHUNKS); ++c) {
         const uint32_t r0 = row0 + c * 32;
         if (r0 >= p.n_rows) break;
         uint32_t m = p.pass ? __ldg(p.pass + (r0 >> 5)) : 0xFFFFFFFFu;
@@ -479,7 +481,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         const uint32_t key = xj == -INFINITY ? 0u : score_key(xj);
         if (key > published) {
           published = key;
-          p.pub[size_t(slice * 2 + chalf) * p.n_queries + qi] = key;
+          p.pub[size_t(slice * EPI_PARTS + chalf) * p.n_queries + qi] = key;
         }
       }
     }
@@ -497,7 +499,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t f_half = __shfl_sync(0xFFFFFFFFu, half, f);
       const float* ls = Lw_s + (size_t(f) * 2 + f_half) * p.k;
       const uint32_t* lr = Lw_r + (size_t(f) * 2 + f_half) * p.k;
-      const size_t base = ((size_t(slice) * 2 + chalf) * p.n_queries + fq) * p.k;
+      const size_t base = ((size_t(slice) * EPI_PARTS + chalf) * p.n_queries + fq) * p.k;
       for (uint32_t i = lane; i < p.k; i += 32) {
         p.part_s[base + i] = i < f_cnt ? ls[i] : -INFINITY;
         const uint32_t r = i < f_cnt ? lr[i] : 0u;
@@ -514,7 +516,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 // ------------------------------------------------------------------ merge
 constexpr uint32_t MERGE_N = 4096;
 constexpr uint32_t MERGE_THREADS = 512;
-constexpr uint32_t kMaxListsMerge = 511;  // partial lists per query in append mode
+constexpr uint32_t kMaxListsMerge = 1023;  // partial lists per query in append mode
 
 __device__ __forceinline__ bool better64(float as, int64_t ai, float bs, int64_t bi)
 {
@@ -940,10 +942,10 @@ static void run_topk_core(const uint16_t* d_db, const float* norms, uint64_t n_r
   const uint32_t tps = div_up(n_tiles, std::min<uint32_t>(want_slices, n_tiles));
   const uint32_t slices = div_up(n_tiles, tps);
   const size_t ctas = size_t(qtiles) * slices;
-  const size_t list_b = ctas * 2 * 2 * k * BM * 4;
-  const size_t part_b = size_t(slices) * 2 * n_queries * k;
+  const size_t list_b = ctas * EPI_PARTS * 2 * k * BM * 4;
+  const size_t part_b = size_t(slices) * EPI_PARTS * n_queries * k;
   const size_t cbuf_b = ctas * EPI * BUF * 4;
-  const uint32_t n_lists = slices * 2;
+  const uint32_t n_lists = slices * EPI_PARTS;
   const size_t pub_b = size_t(n_queries) * n_lists * 4;
   const uint32_t jth = (k + n_lists - 1) / n_lists;
   // Append mode needs the register-tracked list bounds (jth <= 3); its
@@ -1003,7 +1005,7 @@ static void run_topk_core(const uint16_t* d_db, const float* norms, uint64_t n_r
                  DIM, d_out_dist, d_out_ids, s, tp.cand_cnt, cap, tp.cand_r, row_map, row_offset, tp.pub,
                  n_lists, tp.n_rows);
   else
-    merge_launch(tp.part_s, tp.part_id, slices * 2, n_queries, k, metric, 0,
+    merge_launch(tp.part_s, tp.part_id, slices * EPI_PARTS, n_queries, k, metric, 0,
                  reinterpret_cast<const __half*>(d_queries), DIM, d_out_dist, d_out_ids, s);
   uint32_t h_err = 0;
   CR_CUDA(cudaMemcpyAsync(&h_err, tp.err, 4, cudaMemcpyDeviceToHost, s));
