@@ -243,8 +243,42 @@ def run_reference(args):
 
 # ------------------------------------------------------------ secondary
 
+
+def c2_upload_ids(torch, g, dev):
+    """16,384 chunks over 2^30 in thirds (chunk % 3): sparse
+    (2,000 random lows, ARRAY), dense (Bernoulli 0.3, BITMAP), runs (lengths
+    and gaps uniform in [256, 8192], RUN); +5% duplicates; shuffled."""
+    n_chunks = 16384
+    keys = torch.arange(n_chunks, device=dev)
+    sp = keys[keys % 3 == 0]
+    ids_sparse = (sp[:, None] * 65536 + torch.randint(0, 65536, (sp.numel(), 2000), device=dev, generator=g)).flatten()
+    parts = [ids_sparse]
+    de = keys[keys % 3 == 1]
+    for blk in de.split(512):
+        m = torch.rand((blk.numel(), 65536), device=dev, generator=g) < 0.3
+        r, c = torch.nonzero(m, as_tuple=True)
+        parts.append(blk[r] * 65536 + c)
+    ru = keys[keys % 3 == 2]
+    ln = torch.randint(256, 8193, (ru.numel(), 24), device=dev, generator=g)
+    gp = torch.randint(256, 8193, (ru.numel(), 24), device=dev, generator=g)
+    start = torch.cumsum(gp + ln, dim=1) - ln  # run i starts after its gap
+    st = start.flatten()
+    le = ln.flatten()
+    kk = ru.repeat_interleave(24)
+    ok = st < 65536
+    st, le, kk = st[ok], le[ok], kk[ok]
+    le = torch.minimum(le, 65536 - st)
+    off = torch.repeat_interleave(torch.arange(le.numel(), device=dev), le)
+    pos = torch.arange(off.numel(), device=dev) - torch.repeat_interleave(torch.cumsum(le, 0) - le, le)
+    parts.append(kk[off] * 65536 + st[off] + pos)
+    ids = torch.cat(parts)
+    ids = torch.cat([ids, ids[: ids.numel() // 20]])
+    ids = ids[torch.randperm(ids.numel(), device=dev, generator=g)]
+    return ids.to(torch.int32)
+
 def secondary_metrics(torch, cr, pk):
-    """contains Gq/s (config 4 shape) and AND set-op GB/s (config 3 shape), rank 0."""
+    """Rank 0, N=1: contains Gq/s (config 4 shape), AND set-op GB/s,
+    upload (config 2) and multi_and / to_csr (config 3)."""
     out = {}
     dev = "cuda"
     U = 1 << 30
@@ -306,6 +340,88 @@ def secondary_metrics(torch, cr, pk):
     a.free()
     b.free()
     cr.profile_enable(False)
+    # ---- config 2: upload from unsorted device IDs and from the bitset
+    ids = c2_upload_ids(torch, g, dev)
+    n_ids = ids.numel()
+    up = {}
+    for name, thr in (("PROMOTE_AUTO", cr.PROMOTE_AUTO), ("PROMOTE_ALL", cr.PROMOTE_ALL)):
+        for _ in range(2):
+            cr.upload_from_ids(ids, U, bitmap_threshold=thr).free()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(5):
+            t0 = time.perf_counter()
+            b = cr.upload_from_ids(ids, U, bitmap_threshold=thr)
+            torch.cuda.synchronize()
+            ts.append(time.perf_counter() - t0)
+            meta = (b.raw.n_array_containers, b.raw.n_bitmap_containers, b.raw.n_run_containers)
+            if _ < 4:
+                b.free()
+        t = float(np.median(ts))
+        up[name] = {"ms": t * 1e3, "ids_per_s": n_ids / t, "GBps_ids_read": n_ids * 4 / t / 1e9,
+                    "containers_array_bitmap_run": meta}
+    words = cr.decompress_to_bitset(b)
+    b.free()
+    del ids
+    ts = []
+    for _ in range(5):
+        t0 = time.perf_counter()
+        bb = cr.upload_from_device_bitset(words, U, bitmap_threshold=cr.PROMOTE_AUTO)
+        torch.cuda.synchronize()
+        ts.append(time.perf_counter() - t0)
+        bb.free()
+    t = float(np.median(ts))
+    up["from_device_bitset_AUTO"] = {"ms": t * 1e3, "GBps_bitset_read": U / 8 / t / 1e9}
+    del words
+    out["upload_c2"] = {"n_ids": n_ids, "universe": U, **up,
+                        "note": "API time incl. its one host sync; generators give ~3e8 IDs (see SURVEY 8d)"}
+    # ---- config 3: multi_and over 3 / 5 / 8 predicates, to_csr of the result
+    bms = []
+    for p_ in (0.5, 0.1, 0.01, 0.001):
+        w = (torch.rand(U // 32, 32, device=dev, generator=g) < p_)
+        w = (w.int() << torch.arange(32, device=dev, dtype=torch.int32)).sum(dim=1).to(torch.int32)
+        bms.append(cr.upload_from_device_bitset(w, U))
+        del w
+    for _ in range(2):  # clustered runs at ~20%: run lengths [1, 8192], gaps 4x longer on average
+        ln = torch.randint(1, 8193, (70000,), device=dev, generator=g)
+        gp = torch.randint(1, 32769, (70000,), device=dev, generator=g)
+        st = torch.cumsum(gp + ln, 0) - ln
+        ok = st + ln <= U
+        st, ln = st[ok], ln[ok]
+        off = torch.repeat_interleave(torch.arange(ln.numel(), device=dev), ln)
+        pos = torch.arange(off.numel(), device=dev) - torch.repeat_interleave(torch.cumsum(ln, 0) - ln, ln)
+        bms.append(cr.upload_from_ids((st[off] + pos).to(torch.int32), U))
+    rng = np.random.default_rng(5)
+    for _ in range(2):  # Zipf(1.1) ranks, spread by an odd multiplier mod 2^30, ~1% density target
+        z = rng.zipf(1.1, 10_700_000)
+        z = z[z < U].astype(np.uint64)
+        idz = ((z * 2654435761) % U).astype(np.uint32)
+        bms.append(cr.upload_from_ids(torch.from_numpy(idz.view(np.int32)).to(dev), U))
+    ma = {}
+    for cnt in (3, 5, 8):
+        sel = bms[:cnt]
+        for _ in range(2):
+            cr.multi_and(sel).free()
+        ts = []
+        for _ in range(5):
+            t0 = time.perf_counter()
+            r = cr.multi_and(sel)
+            torch.cuda.synchronize()
+            ts.append(time.perf_counter() - t0)
+            if _ < 4:
+                r.free()
+        tcsr = []
+        for _ in range(3):
+            t0 = time.perf_counter()
+            cr.enumerate_ids(r, dtype="uint32")
+            torch.cuda.synchronize()
+            tcsr.append(time.perf_counter() - t0)
+        ma[str(cnt)] = {"ms": float(np.median(ts)) * 1e3, "result_card": int(r.raw.total_cardinality),
+                        "to_csr_ms": float(np.median(tcsr)) * 1e3}
+        r.free()
+    for b_ in bms:
+        b_.free()
+    out["multi_and_c3"] = ma
     return out
 
 
