@@ -58,6 +58,49 @@ __global__ void __launch_bounds__(256) k_contains(cu_roaring::GpuRoaringView v,
   }
 }
 
+// Bulk contains for an all-BITMAP layout (key_index present, container i at
+// slot i): branch-free, kMLP candidates per thread with all key_index loads
+// issued before all bitmap-word loads, so each thread keeps 2 x kMLP
+// independent memory accesses in flight instead of a dependent pair.
+constexpr int kMLP = 8;
+
+__global__ void __launch_bounds__(256) k_contains_bitmap(const uint16_t* __restrict__ key_index,
+                                                         uint32_t max_key,
+                                                         const uint64_t* __restrict__ bitmap,
+                                                         uint32_t negated,
+                                                         const uint32_t* __restrict__ ids, uint64_t n,
+                                                         uint32_t* __restrict__ out)
+{
+  const uint32_t lane = threadIdx.x & 31;
+  const uint64_t n_words = (n + 31) / 32;
+  const uint64_t warp = (uint64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const uint64_t n_warps = (uint64_t(gridDim.x) * blockDim.x) >> 5;
+  for (uint64_t w0 = warp * kMLP; w0 < n_words; w0 += n_warps * kMLP) {
+    uint32_t id[kMLP], idx[kMLP];
+    uint64_t word[kMLP];
+#pragma unroll
+    for (int u = 0; u < kMLP; ++u) {
+      const uint64_t i = (w0 + u) * 32 + lane;
+      id[u] = i < n ? __ldcs(ids + i) : 0u;
+    }
+#pragma unroll
+    for (int u = 0; u < kMLP; ++u) {
+      const uint32_t key = id[u] >> 16;
+      idx[u] = key <= max_key ? uint32_t(__ldg(key_index + key)) : 0xFFFFu;
+    }
+#pragma unroll
+    for (int u = 0; u < kMLP; ++u)
+      word[u] = idx[u] != 0xFFFFu ? __ldg(bitmap + (size_t(idx[u]) << 10) + ((id[u] & 0xFFFFu) >> 6)) : 0ull;
+#pragma unroll
+    for (int u = 0; u < kMLP; ++u) {
+      const uint64_t i = (w0 + u) * 32 + lane;
+      const bool in = (idx[u] != 0xFFFFu) && ((word[u] >> (id[u] & 63u)) & 1ull);
+      const uint32_t bits = __ballot_sync(0xFFFFFFFFu, (in != (negated != 0)) && i < n);
+      if (lane == 0 && w0 + u < n_words) __stcs(out + w0 + u, bits);
+    }
+  }
+}
+
 // One CTA (256 threads) per output chunk.
 __global__ void __launch_bounds__(256) k_decompress(DevBitmap b, uint32_t* out, uint64_t out_words)
 {
@@ -262,8 +305,16 @@ extern "C" int cr_contains_batch(const cr_gpu_roaring* bm, const uint32_t* d_ids
   const uint64_t want = (words + 8 * kUnroll - 1) / (8 * kUnroll);
   const int grid = static_cast<int>(std::max<uint64_t>(1, std::min<uint64_t>(want, uint64_t(sm_count()) * 8)));
   ProfileScope prof(CR_KERNEL_CONTAINS, s);
-  if (mode) k_contains<1><<<grid, 256, 0, s>>>(v, d_ids, n, d_out_bits);
-  else k_contains<0><<<grid, 256, 0, s>>>(v, d_ids, n, d_out_bits);
+  if (mode == 0 && v.all_bitmap) {
+    const uint64_t want_b = (words + 8 * kMLP - 1) / (8 * kMLP);
+    const int grid_b = static_cast<int>(std::max<uint64_t>(1, std::min<uint64_t>(want_b, uint64_t(sm_count()) * 8)));
+    k_contains_bitmap<<<grid_b, 256, 0, s>>>(v.key_index, v.max_key, v.bitmap_data, v.negated ? 1u : 0u,
+                                             d_ids, n, d_out_bits);
+  } else if (mode) {
+    k_contains<1><<<grid, 256, 0, s>>>(v, d_ids, n, d_out_bits);
+  } else {
+    k_contains<0><<<grid, 256, 0, s>>>(v, d_ids, n, d_out_bits);
+  }
   CR_CUDA(cudaGetLastError());
   CR_API_END
 }

@@ -217,7 +217,32 @@ __global__ void __launch_bounds__(256) k_execute(const Operands* __restrict__ op
   const bool and_sub = ops.mode == MODE_AND_SUB;
 #pragma unroll
   for (int i = 0; i < 4; ++i) acc[i] = and_sub ? ~0ull : 0ull;
-  for (uint32_t j = 0; j < ops.np; ++j) {
+  // Fast path for two operands that are both BITMAP containers here (every
+  // set_operation on promoted layouts): both operands' 16-byte loads are
+  // issued before combining, instead of waiting on one operand at a time.
+  bool done = false;
+  if (ops.np + ops.nn == 2) {
+    const int ia = dev_lookup(ops.op[0], key), ib = dev_lookup(ops.op[1], key);
+    if (ia >= 0 && ib >= 0) {
+      const ContainerRef ca = dev_container(ops.op[0], ia), cb = dev_container(ops.op[1], ib);
+      if (ca.type == kBitmap && cb.type == kBitmap) {
+        const uint4* qa = reinterpret_cast<const uint4*>(ops.op[0].bitmap + (ca.off >> 3)) + 2 * t;
+        const uint4* qb = reinterpret_cast<const uint4*>(ops.op[1].bitmap + (cb.off >> 3)) + 2 * t;
+        const uint4 a0 = __ldg(qa), a1 = __ldg(qa + 1), b0 = __ldg(qb), b1 = __ldg(qb + 1);
+        const uint64_t av[4] = {uint64_t(a0.x) | (uint64_t(a0.y) << 32), uint64_t(a0.z) | (uint64_t(a0.w) << 32),
+                                uint64_t(a1.x) | (uint64_t(a1.y) << 32), uint64_t(a1.z) | (uint64_t(a1.w) << 32)};
+        const uint64_t bv[4] = {uint64_t(b0.x) | (uint64_t(b0.y) << 32), uint64_t(b0.z) | (uint64_t(b0.w) << 32),
+                                uint64_t(b1.x) | (uint64_t(b1.y) << 32), uint64_t(b1.z) | (uint64_t(b1.w) << 32)};
+        const bool b_neg = ops.np == 1;  // ANDNOT: the second operand is subtracted
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          acc[i] = b_neg ? (av[i] & ~bv[i])
+                         : (and_sub ? (av[i] & bv[i]) : (ops.mode == MODE_OR ? (av[i] | bv[i]) : (av[i] ^ bv[i])));
+        done = true;
+      }
+    }
+  }
+  for (uint32_t j = 0; j < (done ? 0u : ops.np); ++j) {
     const DevBitmap& b = ops.op[j];
     const int idx = dev_lookup(b, key);
     if (idx < 0) continue;
@@ -226,7 +251,7 @@ __global__ void __launch_bounds__(256) k_execute(const Operands* __restrict__ op
     for (int i = 0; i < 4; ++i)
       acc[i] = and_sub ? (acc[i] & w[i]) : (ops.mode == MODE_OR ? (acc[i] | w[i]) : (acc[i] ^ w[i]));
   }
-  for (uint32_t j = ops.np; j < ops.np + ops.nn; ++j) {
+  for (uint32_t j = ops.np; j < (done ? 0u : ops.np + ops.nn); ++j) {
     const DevBitmap& b = ops.op[j];
     const int idx = dev_lookup(b, key);
     if (idx < 0) continue;
