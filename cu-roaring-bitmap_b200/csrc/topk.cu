@@ -633,13 +633,21 @@ __global__ void __launch_bounds__(MERGE_THREADS) k_merge(const float* part_s, co
     // per-list counts in shared memory, flattened index -> (list, entry).
     __shared__ uint32_t s_pre[kMaxListsMerge + 1];
     const uint32_t nl = total ? n_lists : 0u;
-    if (threadIdx.x == 0) {
-      uint32_t acc = 0;
-      for (uint32_t l = 0; l < nl; ++l) {
-        s_pre[l] = acc;
-        acc += cand_cnt[size_t(q) * n_lists + l];
+    if (threadIdx.x < 32) {  // warp scan of the per-list counts, 32 lists per step
+      uint32_t carry = 0;
+      for (uint32_t l0 = 0; l0 < nl; l0 += 32) {
+        const uint32_t l = l0 + threadIdx.x;
+        const uint32_t c = l < nl ? cand_cnt[size_t(q) * n_lists + l] : 0u;
+        uint32_t x = c;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, x, o);
+          if (threadIdx.x >= o) x += y;
+        }
+        if (l < nl) s_pre[l] = carry + x - c;
+        carry += __shfl_sync(0xFFFFFFFFu, x, 31);
       }
-      s_pre[nl] = acc;
+      if (threadIdx.x == 0) s_pre[nl] = carry;
     }
     __syncthreads();
     const uint32_t n_valid = s_pre[nl];
