@@ -489,12 +489,17 @@ def main():
         dist.barrier()
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    kernel_ms = []
+    kernel_ms, merge_ms, gather_ms = [], [], []
     with ClockSampler(local) as clocks:
         ev0.record(stream)
         for _ in range(args.steps):
             step(queries)
             kernel_ms.append(cr.profile_last_ms(cr.KERNEL_TOPK))
+            try:
+                merge_ms.append(cr.profile_last_ms(cr.KERNEL_TOPK_MERGE))
+                gather_ms.append(cr.profile_last_ms(cr.KERNEL_TOPK_GATHER))
+            except RuntimeError:
+                pass
         ev1.record(stream)
         torch.cuda.synchronize()
         if world > 1:
@@ -573,6 +578,8 @@ def main():
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": None,
                          "kernel": "k_topk", "kernel_ms": kern_ms,
+                         "other_kernels_ms": {"k_merge": float(np.mean(merge_ms)) if merge_ms else None,
+                                              "k_gather_rows": float(np.mean(gather_ms)) if gather_ms else None},
                          "algorithmic": "2*Q*rows_searched*128 flops per launch",
                          "rows_searched": rows_searched,
                          "dense_equivalent_tflops": 2.0 * N_QUERIES * rows_local * DIM / (kern_ms / 1e3) / 1e12,

@@ -904,6 +904,7 @@ void merge_launch(const float* ps, const int64_t* pid, uint32_t parts, uint32_t 
   std::call_once(once, [&] {
     cudaFuncSetAttribute(k_merge, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   });
+  ProfileScope prof(CR_KERNEL_TOPK_MERGE, s);
   k_merge<<<nq, MERGE_THREADS, smem, s>>>(ps, pid, parts, nq, k, metric, kind, queries, dim, od, oi,
                                           cand_cnt, cap, cand_r, row_map, row_offset, pub, n_lists, n_rows);
   CR_CUDA(cudaGetLastError());
@@ -1113,10 +1114,13 @@ extern "C" int cr_filtered_topk(const uint16_t* d_db, const float* d_db_norms, u
       (reinterpret_cast<uintptr_t>(idx + n_pass) + 255) & ~uintptr_t(255));
   float* comp_norms = l2 ? reinterpret_cast<float*>(comp + size_t(n_pass) * DIM) : nullptr;
   k_pass_compact<<<n_wtiles, kWordTile, 0, s>>>(pass, pass_words, tiles, n_wtiles, idx, d_total);
-  k_gather_rows<<<div_up(uint64_t(n_pass) * 16, 256), 256, 0, s>>>(
-      reinterpret_cast<const uint4*>(d_db), idx, n_pass, reinterpret_cast<uint4*>(comp), l2 ? norms : nullptr,
-      comp_norms);
-  CR_CUDA(cudaGetLastError());
+  {
+    ProfileScope prof_g(CR_KERNEL_TOPK_GATHER, s);
+    k_gather_rows<<<div_up(uint64_t(n_pass) * 16, 256), 256, 0, s>>>(
+        reinterpret_cast<const uint4*>(d_db), idx, n_pass, reinterpret_cast<uint4*>(comp), l2 ? norms : nullptr,
+        comp_norms);
+    CR_CUDA(cudaGetLastError());
+  }
   run_topk_core(comp, comp_norms, n_pass, nullptr, idx, d_queries, n_queries, row_offset, k, metric,
                 d_out_dist, d_out_ids, s);
   CR_API_END
