@@ -93,6 +93,8 @@ struct TopkParams {
   float* cand_s;         // [Q][n_lists][cap]
   uint32_t* cand_r;
   uint32_t* cand_cnt;    // [Q][n_lists] entries appended (may exceed cap: overflow)
+  const uint32_t* gather;   // non-null: row r of the search is gather_db row gather[r], copied
+  const uint16_t* gather_db;  // by the producer warp (cp.async) instead of a tiled TMA box
 };
 
 constexpr uint32_t kErrOverflow = 64u;  // a candidate array filled up (append mode)
@@ -236,7 +238,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (uint32_t s = 0; s < STAGES; ++s) { mbar_init(full + s, 1); mbar_init(empty + s, 1); }
+    for (uint32_t s = 0; s < STAGES; ++s) { mbar_init(full + s, p.gather ? 32 : 1); mbar_init(empty + s, 1); }
     for (uint32_t a = 0; a < 2; ++a) { mbar_init(acc_full + a, 1); mbar_init(acc_empty + a, EPI_WARPS); }
     fence_mbar_init();
     *s_done = 0;
@@ -250,7 +252,49 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (warp == 0) {
     // ---------------- TMA producer
-    if (lane == 0) {
+    if (p.gather) {
+      // Whole warp: each instruction copies two 256-byte rows of the tile as
+      // 16-byte chunks into the 128-byte-swizzled K-major layout
+      // (chunk c of a 64-dim half at c ^ (row & 7)). Every lane's copies
+      // arrive on the full barrier when they land (32 arrivals); the MMA
+      // thread fences to the async proxy before reading. Rows past the last
+      // repeat a valid row; the epilogue masks them.
+      if (lane == 0) {
+        prefetch_tmap(&tq);
+        mbar_expect_tx(q_full, 2 * KB_BYTES_Q);
+        tma_load_2d(&tq, q_full, sQ, 0, int32_t(qt * BM));
+        tma_load_2d(&tq, q_full, sQ + KB_BYTES_Q, 64, int32_t(qt * BM));
+      }
+      const uint32_t last = p.n_rows - 1;
+      const uint4* gdb = reinterpret_cast<const uint4*>(p.gather_db);
+      uint32_t yn[8];
+      auto load_idx = [&](uint32_t it) {
+        const uint32_t t = tile_of(min(it, n_it - 1));
+#pragma unroll
+        for (int j = 0; j < 8; ++j) yn[j] = __ldg(p.gather + min(t * BN + lane + 32 * j, last));
+      };
+      load_idx(0);
+      for (uint32_t it = 0; it < n_it; ++it) {
+        const uint32_t s = it % STAGES;
+        uint32_t y[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) y[j] = yn[j];
+        load_idx(it + 1);
+        if (!mbar_wait(empty + s, ((it / STAGES) & 1u) ^ 1u, p.err, 1u)) break;
+        uint8_t* st = sDB + s * STAGE_BYTES;
+        // One instruction moves two whole rows: lane = (row parity, chunk).
+        const uint32_t h = lane >> 4, cc = lane & 15;
+        uint8_t* dcol = st + (cc >> 3) * KB_BYTES_DB;
+#pragma unroll
+        for (uint32_t i = 0; i < BN / 2; ++i) {
+          const uint32_t row = 2 * i + h;
+          const uint32_t src_row = __shfl_sync(0xFFFFFFFFu, y[i >> 4], row & 31);
+          cp_async16(dcol + row * 128 + (((cc & 7) ^ (row & 7)) << 4), gdb + size_t(src_row) * 16 + cc);
+        }
+        cp_async_arrive_noinc(full + s);
+      }
+      cp_async_wait<0>();
+    } else if (lane == 0) {
       prefetch_tmap(&tq);
       prefetch_tmap(&tdb);
       mbar_expect_tx(q_full, 2 * KB_BYTES_Q);
@@ -274,6 +318,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         const uint32_t s = it % STAGES, a = it & 1u;
         if (!mbar_wait(full + s, (it / STAGES) & 1u, p.err, 4u)) break;
         if (!mbar_wait(acc_empty + a, ((it >> 1) & 1u) ^ 1u, p.err, 8u)) break;
+        if (p.gather) fence_proxy_async_smem();  // stage written by cp.async (generic proxy)
         tc_fence_after();
         const uint32_t adb = smem_addr(sDB + s * STAGE_BYTES);
 #pragma unroll
@@ -622,15 +667,9 @@ __global__ void __launch_bounds__(MERGE_THREADS) k_merge(const float* part_s, co
     id[slot] = i;
   };
   if (kind == 2) {
-    // Stream the candidates; only those at or above the bound are kept,
-    // compacted into the free slots [k, MERGE_N), sorted when full.
+    // Per-list counts -> prefix in shared memory (flattened candidate index
+    // -> (list, entry)).
     __shared__ uint32_t s_fill;
-    for (uint32_t i = threadIdx.x; i < MERGE_N; i += MERGE_THREADS) { s[i] = -INFINITY; id[i] = -1; }
-    if (threadIdx.x == 0) s_fill = 0;
-    __syncthreads();
-    constexpr uint32_t B = 2 * MERGE_THREADS;
-    // One pass over the filled part of every list region: prefix of the
-    // per-list counts in shared memory, flattened index -> (list, entry).
     __shared__ uint32_t s_pre[kMaxListsMerge + 1];
     const uint32_t nl = total ? n_lists : 0u;
     if (threadIdx.x < 32) {  // warp scan of the per-list counts, 32 lists per step
@@ -649,37 +688,156 @@ __global__ void __launch_bounds__(MERGE_THREADS) k_merge(const float* part_s, co
       }
       if (threadIdx.x == 0) s_pre[nl] = carry;
     }
+    if (threadIdx.x == 0) s_fill = 0;
     __syncthreads();
     const uint32_t n_valid = s_pre[nl];
-    for (uint32_t c0 = 0; c0 < n_valid; c0 += B) {
-      if (s_fill + B > MERGE_N - k) {
-        bitonic_sort(s, id);
-        for (uint32_t i = k + threadIdx.x; i < MERGE_N; i += MERGE_THREADS) { s[i] = -INFINITY; id[i] = -1; }
-        __syncthreads();
-        if (threadIdx.x == 0) s_fill = 0;
-        __syncthreads();
+    // Candidate c: its score and final id; false when below the bound.
+    auto fetch = [&](uint32_t c, float& x, int64_t& gid) {
+      uint32_t lo = 0, hi = nl;  // last list whose prefix <= c
+      while (hi - lo > 1) {
+        const uint32_t mid = (lo + hi) >> 1;
+        if (s_pre[mid] <= c) lo = mid; else hi = mid;
       }
-      for (uint32_t c = c0 + threadIdx.x; c < min(n_valid, c0 + B); c += MERGE_THREADS) {
-        uint32_t lo = 0, hi = nl;  // last list whose prefix <= c
-        while (hi - lo > 1) {
-          const uint32_t mid = (lo + hi) >> 1;
-          if (s_pre[mid] <= c) lo = mid; else hi = mid;
+      const size_t g = (size_t(q) * n_lists + lo) * cap + (c - s_pre[lo]);
+      x = part_s[g];
+      const uint32_t r = cand_r[g];
+      if (!(x >= bound && r < n_rows)) return false;
+      gid = int64_t(row_map ? __ldg(row_map + r) : r) + int64_t(row_offset);
+      return true;
+    };
+    // Survivors of the bound into slots [0, MERGE_N); the count may exceed.
+    for (uint32_t c = threadIdx.x; c < n_valid; c += MERGE_THREADS) {
+      float x;
+      int64_t g;
+      if (fetch(c, x, g)) {
+        const uint32_t slot = atomicAdd(&s_fill, 1u);
+        if (slot < MERGE_N) { s[slot] = x; id[slot] = g; }
+      }
+    }
+    __syncthreads();
+    const uint32_t n = s_fill;
+    constexpr uint32_t kSelMax = MERGE_THREADS;  // selected set ranked one per thread
+    if (n <= MERGE_N - kSelMax) {
+      // Radix select (8-bit digits, most significant first) of the k-th best
+      // score key T; the selected set is every survivor with key >= T.
+      __shared__ uint32_t s_hist[256];
+      __shared__ uint32_t s_sel[3];
+      uint32_t thr = 0;
+      if (n > k) {
+        uint32_t prefix = 0, mask = 0, rem = k;
+        for (int shift = 24; shift >= 0; shift -= 8) {
+          for (uint32_t b = threadIdx.x; b < 256; b += MERGE_THREADS) s_hist[b] = 0;
+          __syncthreads();
+          for (uint32_t e = threadIdx.x; e < n; e += MERGE_THREADS) {
+            const uint32_t key = score_key(s[e]);
+            if ((key & mask) == prefix) atomicAdd(&s_hist[(key >> shift) & 255u], 1u);
+          }
+          __syncthreads();
+          if (threadIdx.x < 32) {
+            const uint32_t lane = threadIdx.x;
+            uint32_t cnt[8], tot = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) { cnt[j] = s_hist[255 - (8 * lane + j)]; tot += cnt[j]; }
+            uint32_t x = tot;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+              const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, x, o);
+              if (lane >= o) x += y;
+            }
+            const uint32_t before = x - tot;  // survivors in higher digits
+            if (before < rem && rem <= x) {
+              uint32_t acc = before;
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                if (acc + cnt[j] >= rem) {
+                  s_sel[0] = prefix | (uint32_t(255 - (8 * lane + j)) << shift);
+                  s_sel[1] = rem - acc;
+                  break;
+                }
+                acc += cnt[j];
+              }
+            }
+          }
+          __syncthreads();
+          prefix = s_sel[0];
+          rem = s_sel[1];
+          mask |= 255u << shift;
         }
-        const size_t g = (size_t(q) * n_lists + lo) * cap + (c - s_pre[lo]);
-        const float x = part_s[g];
-        const uint32_t r = cand_r[g];
-        if (x >= bound && r < n_rows) {
-          const uint32_t slot = k + atomicAdd(&s_fill, 1u);
-          s[slot] = x;
-          id[slot] = int64_t(row_map ? __ldg(row_map + r) : r) + int64_t(row_offset);
+        thr = prefix;
+      }
+      // Compact key >= T into the tail slots.
+      __shared__ uint32_t s_m;
+      if (threadIdx.x == 0) s_m = 0;
+      __syncthreads();
+      float* cs = s + (MERGE_N - kSelMax);
+      int64_t* cid = id + (MERGE_N - kSelMax);
+      for (uint32_t e = threadIdx.x; e < n; e += MERGE_THREADS) {
+        if (score_key(s[e]) >= thr) {
+          const uint32_t slot = atomicAdd(&s_m, 1u);
+          if (slot < kSelMax) { cs[slot] = s[e]; cid[slot] = id[e]; }
         }
       }
       __syncthreads();
+      const uint32_t m = s_m;
+      if (m <= kSelMax) {
+        // Exact rank of each selected entry (score desc, id asc); the best k
+        // go straight to their output slots.
+        const float qn = s_qn;
+        if (threadIdx.x < m) {
+          const float x = cs[threadIdx.x];
+          const int64_t g = cid[threadIdx.x];
+          uint32_t rank = 0;
+          for (uint32_t j = 0; j < m; ++j) rank += better64(cs[j], cid[j], x, g) ? 1u : 0u;
+          if (rank < k) {
+            out_d[size_t(q) * k + rank] = l2 ? qn - x : x;
+            out_id[size_t(q) * k + rank] = g;
+          }
+        }
+        for (uint32_t i = m + threadIdx.x; i < k; i += MERGE_THREADS) {
+          out_d[size_t(q) * k + i] = l2 ? INFINITY : -INFINITY;
+          out_id[size_t(q) * k + i] = -1;
+        }
+        return;
+      }
     }
-    // Sort just the occupied prefix (rounded up to a power of two).
-    uint32_t n_sort = 2;
-    while (n_sort < k + s_fill) n_sort <<= 1;
-    bitonic_sort(s, id, min(n_sort, MERGE_N));
+    if (n <= MERGE_N) {
+      // Too many ties at the k-th score for the rank pass: sort the
+      // survivors (already in [0, n)).
+      uint32_t n_sort = 2;
+      while (n_sort < n) n_sort <<= 1;
+      for (uint32_t i = n + threadIdx.x; i < n_sort; i += MERGE_THREADS) { s[i] = -INFINITY; id[i] = -1; }
+      __syncthreads();
+      bitonic_sort(s, id, n_sort);
+    } else {
+      // More survivors than shared memory holds: stream them again,
+      // compacted into the free slots [k, MERGE_N), sorted when full.
+      for (uint32_t i = threadIdx.x; i < MERGE_N; i += MERGE_THREADS) { s[i] = -INFINITY; id[i] = -1; }
+      if (threadIdx.x == 0) s_fill = 0;
+      __syncthreads();
+      constexpr uint32_t B = 2 * MERGE_THREADS;
+      for (uint32_t c0 = 0; c0 < n_valid; c0 += B) {
+        if (s_fill + B > MERGE_N - k) {
+          bitonic_sort(s, id);
+          for (uint32_t i = k + threadIdx.x; i < MERGE_N; i += MERGE_THREADS) { s[i] = -INFINITY; id[i] = -1; }
+          __syncthreads();
+          if (threadIdx.x == 0) s_fill = 0;
+          __syncthreads();
+        }
+        for (uint32_t c = c0 + threadIdx.x; c < min(n_valid, c0 + B); c += MERGE_THREADS) {
+          float x;
+          int64_t g;
+          if (fetch(c, x, g)) {
+            const uint32_t slot = k + atomicAdd(&s_fill, 1u);
+            s[slot] = x;
+            id[slot] = g;
+          }
+        }
+        __syncthreads();
+      }
+      uint32_t n_sort = 2;
+      while (n_sort < k + s_fill) n_sort <<= 1;
+      bitonic_sort(s, id, min(n_sort, MERGE_N));
+    }
   } else {
     uint64_t pos = 0;
     for (uint32_t i = threadIdx.x; i < MERGE_N; i += MERGE_THREADS) load(pos + i, i);
@@ -811,7 +969,8 @@ __global__ void __launch_bounds__(kWordTile) k_pass_tile_sums(const uint32_t* pa
 // idx[] = shard rows whose filter bit is set, ascending; *total = count.
 __global__ void __launch_bounds__(kWordTile) k_pass_compact(const uint32_t* pass, uint64_t n_words,
                                                             const uint32_t* tile_sums, uint32_t n_tiles,
-                                                            uint32_t* idx, uint32_t* total)
+                                                            uint32_t* idx, uint32_t* total,
+                                                            const float* norms, float* comp_norms)
 {
   __shared__ uint32_t s_red[32];
   __shared__ uint32_t s_base;
@@ -830,21 +989,12 @@ __global__ void __launch_bounds__(kWordTile) k_pass_compact(const uint32_t* pass
   uint32_t tot;
   uint32_t pos = s_base + block_exclusive_scan<kWordTile>(uint32_t(__popc(x)), s_red, &tot);
   while (x) {
-    idx[pos++] = uint32_t(w * 32 + __ffs(x) - 1);
+    const uint32_t r = uint32_t(w * 32 + __ffs(x) - 1);
+    idx[pos] = r;
+    if (norms) comp_norms[pos] = __ldg(norms + r);
+    ++pos;
     x &= x - 1;
   }
-}
-
-// comp[i] = db[idx[i]] (16 lanes x 16 B per 128-dim row); norms likewise.
-__global__ void k_gather_rows(const uint4* db, const uint32_t* idx, uint32_t n, uint4* comp,
-                              const float* norms, float* comp_norms)
-{
-  const uint64_t g = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  const uint64_t row = g >> 4;
-  if (row >= n) return;
-  const uint32_t src = __ldg(idx + row);
-  comp[row * 16 + (g & 15)] = __ldcs(db + uint64_t(src) * 16 + (g & 15));
-  if (norms && (g & 15) == 0) comp_norms[row] = __ldg(norms + src);
 }
 
 __global__ void k_fill_empty(float* d, int64_t* ids, uint64_t n, float v)
@@ -938,7 +1088,8 @@ extern "C" int cr_row_norms(const uint16_t* d_db, uint64_t n_rows, uint32_t dim,
 static void run_topk_core(const uint16_t* d_db, const float* norms, uint64_t n_rows, const uint32_t* pass,
                           const uint32_t* row_map, const uint16_t* d_queries, uint32_t n_queries,
                           uint64_t row_offset, uint32_t k, int metric, float* d_out_dist,
-                          int64_t* d_out_ids, cudaStream_t s, bool allow_append = true)
+                          int64_t* d_out_ids, cudaStream_t s, bool allow_append = true,
+                          uint64_t gather_rows = 0)
 {
   static std::once_flag once;
   std::call_once(once, [] {
@@ -1002,7 +1153,11 @@ static void run_topk_core(const uint16_t* d_db, const float* norms, uint64_t n_r
   if (const char* kn = getenv("CR_TOPK_KEEPER_NS")) tp.keeper_ns = uint32_t(atoi(kn));
   CR_CUDA(cudaMemsetAsync(tp.err, 0, 16 + size_t(n_queries) * 4, s));
   const CUtensorMap tq = make_map(d_queries, n_queries, BM);
-  const CUtensorMap tdb = make_map(d_db, n_rows, BN);
+  // Gather mode (gather_rows > 0): d_db holds gather_rows rows and search row
+  // r is d_db row row_map[r].
+  tp.gather = gather_rows ? row_map : nullptr;
+  tp.gather_db = d_db;
+  const CUtensorMap tdb = make_map(d_db, gather_rows ? gather_rows : n_rows, BN);
   {
     ProfileScope prof(CR_KERNEL_TOPK, s);
     if (append) k_topk<true><<<dim3(qtiles, slices), THREADS, SMEM_TOTAL, s>>>(tq, tdb, tp);
@@ -1029,7 +1184,7 @@ static void run_topk_core(const uint16_t* d_db, const float* norms, uint64_t n_r
     // Degenerate score distribution (e.g. massive ties): redo exactly with
     // per-list merging, which needs no candidate capacity.
     run_topk_core(d_db, norms, n_rows, pass, row_map, d_queries, n_queries, row_offset, k, metric,
-                  d_out_dist, d_out_ids, s, false);
+                  d_out_dist, d_out_ids, s, false, gather_rows);
     return;
   }
   if (h_err) fail(CR_ERR_DEVICE, "cr_filtered_topk: pipeline wait timed out (code " + std::to_string(h_err) + ")");
@@ -1107,22 +1262,20 @@ extern "C" int cr_filtered_topk(const uint16_t* d_db, const float* d_db_norms, u
                   d_out_dist, d_out_ids, s);
     return CR_OK;
   }
-  // Pre-filter: gather the passing rows into a dense copy and search that.
-  Scratch comp_scr(size_t(n_pass) * 4 + 256 + size_t(n_pass) * DIM * 2 + (l2 ? size_t(n_pass) * 4 + 16 : 0), s);
+  // Pre-filter: compact the passing rows' indices (and norms) and search
+  // only those rows, fetched from the shard by TMA row gathers.
+  Scratch comp_scr(size_t(n_pass) * 4 + 256 + (l2 ? size_t(n_pass) * 4 : 0), s);
   uint32_t* idx = comp_scr.as<uint32_t>();
-  uint16_t* comp = reinterpret_cast<uint16_t*>(
-      (reinterpret_cast<uintptr_t>(idx + n_pass) + 255) & ~uintptr_t(255));
-  float* comp_norms = l2 ? reinterpret_cast<float*>(comp + size_t(n_pass) * DIM) : nullptr;
-  k_pass_compact<<<n_wtiles, kWordTile, 0, s>>>(pass, pass_words, tiles, n_wtiles, idx, d_total);
+  float* comp_norms = l2 ? reinterpret_cast<float*>(
+      (reinterpret_cast<uintptr_t>(idx + n_pass) + 255) & ~uintptr_t(255)) : nullptr;
   {
-    ProfileScope prof_g(CR_KERNEL_TOPK_GATHER, s);
-    k_gather_rows<<<div_up(uint64_t(n_pass) * 16, 256), 256, 0, s>>>(
-        reinterpret_cast<const uint4*>(d_db), idx, n_pass, reinterpret_cast<uint4*>(comp), l2 ? norms : nullptr,
-        comp_norms);
+    ProfileScope prof_c(CR_KERNEL_TOPK_COMPACT, s);
+    k_pass_compact<<<n_wtiles, kWordTile, 0, s>>>(pass, pass_words, tiles, n_wtiles, idx, d_total,
+                                                  l2 ? norms : nullptr, comp_norms);
     CR_CUDA(cudaGetLastError());
   }
-  run_topk_core(comp, comp_norms, n_pass, nullptr, idx, d_queries, n_queries, row_offset, k, metric,
-                d_out_dist, d_out_ids, s);
+  run_topk_core(d_db, comp_norms, n_pass, nullptr, idx, d_queries, n_queries, row_offset, k, metric,
+                d_out_dist, d_out_ids, s, true, n_rows);
   CR_API_END
 }
 

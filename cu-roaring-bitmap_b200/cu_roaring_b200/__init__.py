@@ -382,7 +382,7 @@ def topk_merge(dist_parts, id_parts, k: int, metric: int = METRIC_IP, stream=Non
 # ------------------------------------------------------------- measurement
 
 (KERNEL_TOPK, KERNEL_CONTAINS, KERNEL_SETOP, KERNEL_UPLOAD_SCATTER, KERNEL_UPLOAD_EMIT, KERNEL_DECOMPRESS,
- KERNEL_TOPK_MERGE, KERNEL_TOPK_GATHER) = range(8)
+ KERNEL_TOPK_MERGE, KERNEL_TOPK_COMPACT) = range(8)
 
 
 def profile_enable(on: bool = True) -> None:

@@ -211,7 +211,7 @@ int cr_topk_merge(const float* d_dist_parts, const int64_t* d_id_parts, uint32_t
  * the launching stream; cr_profile_last_ms returns the device time of the
  * most recent launch of `kernel` on the calling thread (waits for it).
  * Kernel ids: CR_KERNEL_TOPK, CR_KERNEL_CONTAINS, CR_KERNEL_SETOP, CR_KERNEL_UPLOAD_SCATTER,
- * CR_KERNEL_UPLOAD_EMIT, CR_KERNEL_DECOMPRESS, CR_KERNEL_TOPK_MERGE, CR_KERNEL_TOPK_GATHER. */
+ * CR_KERNEL_UPLOAD_EMIT, CR_KERNEL_DECOMPRESS, CR_KERNEL_TOPK_MERGE, CR_KERNEL_TOPK_COMPACT. */
 #define CR_KERNEL_TOPK 0
 #define CR_KERNEL_CONTAINS 1
 #define CR_KERNEL_SETOP 2
@@ -219,7 +219,7 @@ int cr_topk_merge(const float* d_dist_parts, const int64_t* d_id_parts, uint32_t
 #define CR_KERNEL_UPLOAD_EMIT 4
 #define CR_KERNEL_DECOMPRESS 5
 #define CR_KERNEL_TOPK_MERGE 6
-#define CR_KERNEL_TOPK_GATHER 7
+#define CR_KERNEL_TOPK_COMPACT 7
 int cr_profile_enable(int on);
 int cr_profile_last_ms(int kernel, float* ms);
 

@@ -173,3 +173,30 @@ def test_topk_filter_container_kinds(cr, oracle, torch_, kind):
                             k, metric=0, filter=filt, row_offset=lo)
     check_topk(d.cpu().numpy(), i.cpu().numpy(), d_ref, i_ref, 0)
     filt.free()
+
+
+@pytest.mark.parametrize("n_dup", [60, 600])
+def test_topk_duplicate_rows_tie_break(cr, oracle, torch_, n_dup):
+    """n_dup copies of query 0's own vector planted among random rows: for
+    query 0 they tie for first place and the smallest ids of them must come
+    out, in id order. 600 copies exceed the exact-rank pass of the merge and
+    take its sorting fallback; 60 copies stay on the rank pass."""
+    n, q, k = 60_000, 64, 100
+    db, qs = make_data(n, q, seed=21)
+    rng = np.random.default_rng(22)
+    dup = np.sort(rng.choice(n, n_dup, replace=False))
+    db[dup] = qs[0]
+    ids = np.flatnonzero(rng.random(n) < 0.3).astype(np.uint32)
+    ids = np.union1d(ids, dup).astype(np.uint32)
+    filt = cr.upload_from_ids(ids, n)
+    words = np.zeros((n + 31) // 32, dtype=np.uint32)
+    np.bitwise_or.at(words, ids // 32, (1 << (ids % 32)).astype(np.uint32))
+    for metric in (0, 1):
+        d_ref, i_ref = oracle.topk(db, qs, k, metric, words)
+        ddb = torch_.from_numpy(db).cuda()
+        d, i = cr.filtered_topk(ddb, torch_.from_numpy(qs).cuda(), k, metric=metric, filter=filt)
+        i = i.cpu().numpy()
+        m = min(k, n_dup)
+        assert (i[0, :m] == dup[:m]).all()
+        check_topk(d.cpu().numpy(), i, d_ref, i_ref, metric)
+    filt.free()
