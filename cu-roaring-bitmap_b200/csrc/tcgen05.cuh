@@ -77,6 +77,13 @@ __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* ba
       : "memory");
 }
 
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* ptr)
+{
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+  return v;
+}
+
 // 16-byte global -> shared copy through L2 (cp.async, generic proxy).
 __device__ __forceinline__ void cp_async16(void* dst, const void* src)
 {

@@ -28,8 +28,10 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
 #include <mutex>
 #include <vector>
 
@@ -95,9 +97,19 @@ struct TopkParams {
   uint32_t* cand_cnt;    // [Q][n_lists] entries appended (may exceed cap: overflow)
   const uint32_t* gather;   // non-null: row r of the search is gather_db row gather[r], copied
   const uint16_t* gather_db;  // by the producer warp (cp.async) instead of a tiled TMA box
+  // Speculative bound (append mode). A prologue launch (prologue_only) runs
+  // the publish-only tiles and every list writes its best three scores to
+  // pub_top [list * 3 + i][Q]; k_spec turns their union into spec_used [Q];
+  // the main launch (no_prologue) starts with that bound. The merge verifies it.
+  uint32_t prologue_only;
+  uint32_t no_prologue;
+  uint32_t* pub_top;
+  const uint32_t* spec_used;
 };
 
 constexpr uint32_t kErrOverflow = 64u;  // a candidate array filled up (append mode)
+constexpr uint32_t kErrSpec = 128u;
+constexpr uint32_t kPrologueTiles = 4;  // publish-only tiles at the start of each slice (append mode)     // a query's speculative bound was above its k-th best
 
 // Order-preserving map float -> uint32 (larger float -> larger key); 0 is
 // below every real score and decodes to -inf.
@@ -232,8 +244,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   // in publish-only mode (their best scores feed the shared bound, nothing is
   // kept), then every tile runs with the bound, those D last.
   const uint32_t T = t1 - t0;
-  const uint32_t D = APPEND ? min(T, 4u) : 0u;
-  const uint32_t n_it = T + D;
+  const uint32_t D = (APPEND && !p.no_prologue) ? min(T, kPrologueTiles) : 0u;
+  const uint32_t n_it = p.prologue_only ? D : T + D;
   auto tile_of = [&](uint32_t it) { return it < T ? t0 + it : t0 + (it - T); };
 
   if (threadIdx.x == 0) {
@@ -243,7 +255,12 @@ __global__ void __launch_bounds__(THREADS, 1)
     fence_mbar_init();
     *s_done = 0;
   }
-  for (uint32_t i = threadIdx.x; i < BM; i += THREADS) s_bound[i] = -INFINITY;
+  // The shared bound starts at the speculative bound when there is one, so
+  // the first tiles are filtered before the keeper's first refresh.
+  for (uint32_t i = threadIdx.x; i < BM; i += THREADS) {
+    const uint32_t q2 = qt * BM + i;
+    s_bound[i] = (p.spec_used && q2 < p.n_queries) ? key_score(__ldcg(p.spec_used + q2)) : -INFINITY;
+  }
   if (warp == 0) tmem_alloc(tmem_slot, TMEM_COLS);
   tc_fence_before();
   __syncthreads();
@@ -335,9 +352,18 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else if (warp == 2) {
     // ---------------- bound keeper: for each query of the tile, the minimum
     // over all partial lists of their published jth best (a lower bound of
-    // the k-th best, see the epilogue), kept fresh in shared memory.
+    // the k-th best, see the epilogue), kept fresh in shared memory; raised
+    // to the speculative bound once that is known.
+    float spec[BM / 32];
+#pragma unroll
+    for (uint32_t i = 0; i < BM / 32; ++i) {
+      const uint32_t q2 = qt * BM + lane + 32 * i;
+      spec[i] = (p.spec_used && q2 < p.n_queries) ? key_score(__ldcg(p.spec_used + q2)) : -INFINITY;
+    }
     for (uint32_t iter = 0; iter < kSpinLimit; ++iter) {
-      for (uint32_t qq = lane; qq < BM; qq += 32) {
+#pragma unroll
+      for (uint32_t i = 0; i < BM / 32; ++i) {
+        const uint32_t qq = lane + 32 * i;
         const uint32_t q2 = qt * BM + qq;
         if (q2 >= p.n_queries) continue;
         uint32_t m0 = 0xFFFFFFFFu, m1 = 0xFFFFFFFFu, m2 = 0xFFFFFFFFu, m3 = 0xFFFFFFFFu;
@@ -349,7 +375,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           m3 = min(m3, __ldcg(p.pub + size_t(l + 3) * p.n_queries + q2));
         }
         for (; l < p.n_lists; ++l) m0 = min(m0, __ldcg(p.pub + size_t(l) * p.n_queries + q2));
-        s_bound[qq] = key_score(min(min(m0, m1), min(m2, m3)));
+        s_bound[qq] = fmaxf(key_score(min(min(m0, m1), min(m2, m3))), spec[i]);
       }
       if (*reinterpret_cast<volatile uint32_t*>(s_done) >= EPI_WARPS) break;
       __nanosleep(p.keeper_ns);
@@ -423,7 +449,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     // Best three scores this list has taken in (list + buffer), to publish its
     // jth best every tile when jth <= 3 without waiting for a merge.
     float top1 = -INFINITY, top2 = -INFINITY, top3 = -INFINITY;
-    uint32_t published = 0;
+    // A main launch after a prologue launch keeps the prologue's published
+    // values (valid lower bounds) until this list beats them.
+    uint32_t published =
+        (APPEND && p.no_prologue && valid_q) ? __ldcg(p.pub + size_t(slice * EPI_PARTS + chalf) * p.n_queries + qi) : 0u;
     const bool fast_pub = p.jth <= 3;
     const uint32_t my_list = slice * EPI_PARTS + chalf;
     uint32_t nc = 0;  // candidates this (query, list) appended (append mode)
@@ -432,7 +461,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t t = tile_of(it), a = it & 1u;
       const bool publish_only = it < D;
       if (valid_q) {
-        gthr = fmaxf(gthr, key_score(__ldcg(p.shared_thr + qi)));
+        if (!APPEND) gthr = fmaxf(gthr, key_score(__ldcg(p.shared_thr + qi)));  // written by list merges only
         // Every list holds >= jth entries >= its published jth best, and
         // n_lists * jth >= k: the minimum over lists bounds the k-th best.
         gthr = fmaxf(gthr, reinterpret_cast<volatile float*>(s_bound)[t_local]);
@@ -509,7 +538,10 @@ __global__ void __launch_bounds__(THREADS, 1)
               mybuf_r[nb] = r;
               ++nb;
             }
-            if (fast_pub && val > top3) {
+            // Re-run prologue tiles (it >= T) were already counted in the
+            // best three during the prologue; counting them again would let
+            // one row stand for two.
+            if (fast_pub && it < T && val > top3) {
               if (val > top1) { top3 = top2; top2 = top1; top1 = val; }
               else if (val > top2) { top3 = top2; top2 = val; }
               else { top3 = val; }
@@ -521,6 +553,12 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(acc_empty + a);
+      if (APPEND && p.prologue_only && it + 1 == D && valid_q) {
+        const size_t base = size_t(my_list) * 3 * p.n_queries + qi;
+        p.pub_top[base] = top1 == -INFINITY ? 0u : score_key(top1);
+        p.pub_top[base + p.n_queries] = top2 == -INFINITY ? 0u : score_key(top2);
+        p.pub_top[base + 2 * size_t(p.n_queries)] = top3 == -INFINITY ? 0u : score_key(top3);
+      }
       if (fast_pub && valid_q) {
         const float xj = p.jth == 1 ? top1 : (p.jth == 2 ? top2 : top3);
         const uint32_t key = xj == -INFINITY ? 0u : score_key(xj);
@@ -531,7 +569,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
     }
     if (!APPEND) flush(1);
-    if (APPEND && valid_q) {
+    if (APPEND && valid_q && !p.prologue_only) {
       p.cand_cnt[size_t(qi) * p.n_lists + my_list] = nc;
       if (nc > p.cap) atomicOr(p.err, kErrOverflow);
     }
@@ -556,6 +594,31 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, TMEM_COLS);
+}
+
+// One warp per query: spec_used[q] = the j-th largest of the n_vals (<= 256)
+// published keys pub_top[i][q] (0 when fewer than j are non-zero).
+__global__ void __launch_bounds__(128) k_spec(const uint32_t* pub_top, uint32_t n_vals, uint32_t n_queries,
+                                              uint32_t j, uint32_t* spec_used)
+{
+  const uint32_t q = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (q >= n_queries) return;
+  uint32_t v[8];
+#pragma unroll
+  for (uint32_t e = 0; e < 8; ++e) {
+    const uint32_t idx = lane + 32 * e;
+    v[e] = idx < n_vals ? __ldg(pub_top + size_t(idx) * n_queries + q) : 0u;
+  }
+  // Largest key x with at least j keys >= x, one bit at a time.
+  uint32_t x = 0;
+  for (int bit = 31; bit >= 0; --bit) {
+    const uint32_t c = x | (1u << bit);
+    uint32_t n = 0;
+#pragma unroll
+    for (uint32_t e = 0; e < 8; ++e) n += v[e] >= c ? 1u : 0u;
+    if (__reduce_add_sync(0xFFFFFFFFu, n) >= j) x = c;
+  }
+  if (lane == 0) spec_used[q] = x;
 }
 
 // ------------------------------------------------------------------ merge
@@ -600,7 +663,8 @@ __global__ void __launch_bounds__(MERGE_THREADS) k_merge(const float* part_s, co
                                                          const uint32_t* cand_r,
                                                          const uint32_t* row_map, uint64_t row_offset,
                                                          const uint32_t* pub, uint32_t n_lists,
-                                                         uint32_t n_rows)
+                                                         uint32_t n_rows, const uint32_t* spec_used,
+                                                         uint32_t* err)
 {
   extern __shared__ uint8_t smem_raw[];
   float* s = reinterpret_cast<float*>(smem_raw);
@@ -632,6 +696,9 @@ __global__ void __launch_bounds__(MERGE_THREADS) k_merge(const float* part_s, co
     __syncthreads();
     bound = key_score(s_min);
   }
+  // kind 2 with a speculative bound: rows below it were dropped, which is
+  // exact only if the k-th best found is at or above it.
+  const uint32_t spec = (kind == 2 && spec_used) ? spec_used[q] : 0u;
   // kind 2: n_lists regions of `cap` slots per query. An overflowed region
   // has unwritten slots; that pass is redone by the caller, so skip it here.
   __shared__ uint32_t s_over;
@@ -716,6 +783,7 @@ __global__ void __launch_bounds__(MERGE_THREADS) k_merge(const float* part_s, co
     }
     __syncthreads();
     const uint32_t n = s_fill;
+    __syncthreads();  // every thread has n before the fallback below resets s_fill
     constexpr uint32_t kSelMax = MERGE_THREADS;  // selected set ranked one per thread
     if (n <= MERGE_N - kSelMax) {
       // Radix select (8-bit digits, most significant first) of the k-th best
@@ -764,6 +832,9 @@ __global__ void __launch_bounds__(MERGE_THREADS) k_merge(const float* part_s, co
           mask |= 255u << shift;
         }
         thr = prefix;
+        if (threadIdx.x == 0 && thr < spec) atomicOr(err, kErrSpec);
+      } else if (threadIdx.x == 0 && spec && !s_over) {
+        atomicOr(err, kErrSpec);  // fewer than k kept: the bound may have dropped some
       }
       // Compact key >= T into the tail slots.
       __shared__ uint32_t s_m;
@@ -851,6 +922,7 @@ __global__ void __launch_bounds__(MERGE_THREADS) k_merge(const float* part_s, co
       bitonic_sort(s, id);
     }
   }
+  if (threadIdx.x == 0 && spec && (id[k - 1] < 0 || score_key(s[k - 1]) < spec)) atomicOr(err, kErrSpec);
   const float qn = s_qn;
   for (uint32_t i = threadIdx.x; i < k; i += MERGE_THREADS) {
     const int64_t r = id[i];
@@ -1047,7 +1119,7 @@ void merge_launch(const float* ps, const int64_t* pid, uint32_t parts, uint32_t 
                   cudaStream_t s, const uint32_t* cand_cnt = nullptr, uint32_t cap = 0,
                   const uint32_t* cand_r = nullptr, const uint32_t* row_map = nullptr,
                   uint64_t row_offset = 0, const uint32_t* pub = nullptr, uint32_t n_lists = 0,
-                  uint32_t n_rows = 0)
+                  uint32_t n_rows = 0, const uint32_t* spec_used = nullptr, uint32_t* err = nullptr)
 {
   static std::once_flag once;
   const size_t smem = MERGE_N * 12;
@@ -1056,7 +1128,8 @@ void merge_launch(const float* ps, const int64_t* pid, uint32_t parts, uint32_t 
   });
   ProfileScope prof(CR_KERNEL_TOPK_MERGE, s);
   k_merge<<<nq, MERGE_THREADS, smem, s>>>(ps, pid, parts, nq, k, metric, kind, queries, dim, od, oi,
-                                          cand_cnt, cap, cand_r, row_map, row_offset, pub, n_lists, n_rows);
+                                          cand_cnt, cap, cand_r, row_map, row_offset, pub, n_lists, n_rows,
+                                          spec_used, err);
   CR_CUDA(cudaGetLastError());
 }
 
@@ -1089,7 +1162,7 @@ static void run_topk_core(const uint16_t* d_db, const float* norms, uint64_t n_r
                           const uint32_t* row_map, const uint16_t* d_queries, uint32_t n_queries,
                           uint64_t row_offset, uint32_t k, int metric, float* d_out_dist,
                           int64_t* d_out_ids, cudaStream_t s, bool allow_append = true,
-                          uint64_t gather_rows = 0)
+                          uint64_t gather_rows = 0, bool allow_spec = true)
 {
   static std::once_flag once;
   std::call_once(once, [] {
@@ -1113,8 +1186,36 @@ static void run_topk_core(const uint16_t* d_db, const float* norms, uint64_t n_r
   const bool append = allow_append && jth <= 3 && n_lists <= kMaxListsMerge;
   const uint32_t cap = append ? std::max<uint32_t>(256u, div_up(std::max<uint32_t>(32768u, 128u * k), n_lists)) : 0u;
   const size_t cand_b = append ? size_t(n_queries) * n_lists * cap * 4 : 0;
+  // Speculative bound: the prologue sees about `sample` of the rows; the
+  // spec_j-th best of the union of every list's top 3 then has fewer than k
+  // rows at or above it with probability P(Poisson(k * sample / n_rows) >=
+  // spec_j) (taken below 1e-9), each list's top 3 only lowering the value.
+  uint32_t spec_j = 0;
+  if (append && allow_spec && 3 * n_lists <= 256) {
+    const uint64_t sample =
+        std::min<uint64_t>(n_rows, uint64_t(slices) * std::min<uint32_t>(tps, kPrologueTiles) * BN);
+    const double f = double(sample) / double(n_rows);
+    if (f <= 0.5) {
+      const double lam = double(k) * f;
+      // P(X >= j) for X ~ Poisson(lam), summed from j upward.
+      auto tail = [&](uint32_t j) {
+        double term = std::exp(-lam), acc = 0.0;
+        for (uint32_t i = 1; i <= j; ++i) term *= lam / double(i);
+        for (uint32_t i = j; i < j + 400; ++i) { acc += term; term *= lam / double(i + 1); }
+        return acc;
+      };
+      uint32_t j = std::max<uint32_t>(1u, uint32_t(lam));
+      while (j <= 3 * n_lists && tail(j) >= 1e-9) ++j;
+      if (j <= 3 * n_lists) spec_j = j;
+    }
+    // Test hook: force the rank (1 = the sample's best, which is almost
+    // surely above the k-th best and so exercises the verification) or
+    // switch the bound off (0).
+    if (const char* sj = getenv("CR_TOPK_SPEC_J")) spec_j = std::min<uint32_t>(uint32_t(atoi(sj)), 3 * n_lists);
+  }
+  const size_t spec_b = spec_j ? size_t(n_queries) * n_lists * 3 * 4 + size_t(n_queries) * 4 + 16 : 0;
   Scratch scr(list_b * 2 + cbuf_b * 2 + part_b * 12 + pub_b + cand_b * 2 + size_t(n_queries) * n_lists * 4 +
-                  size_t(n_queries) * 8 + 64 + 512, s);
+                  size_t(n_queries) * 8 + 64 + 512 + spec_b, s);
   char* p = scr.as<char>();
   TopkParams tp{};
   tp.n_rows = static_cast<uint32_t>(n_rows);
@@ -1143,6 +1244,12 @@ static void run_topk_core(const uint16_t* d_db, const float* norms, uint64_t n_r
     tp.cand_cnt = reinterpret_cast<uint32_t*>(p); p += size_t(n_queries) * n_lists * 4;
     CR_CUDA(cudaMemsetAsync(tp.cand_cnt, 0, size_t(n_queries) * n_lists * 4, s));
   }
+  uint32_t* spec_used = nullptr;
+  if (spec_j) {
+    tp.pub_top = reinterpret_cast<uint32_t*>(p); p += size_t(n_queries) * n_lists * 3 * 4;
+    spec_used = reinterpret_cast<uint32_t*>(p); p += size_t(n_queries) * 4 + 16;
+    CR_CUDA(cudaMemsetAsync(tp.pub_top, 0, size_t(n_queries) * n_lists * 3 * 4, s));
+  }
   tp.part_id = reinterpret_cast<int64_t*>(p); p += part_b * 8;
   tp.part_s = reinterpret_cast<float*>(p); p += part_b * 4;
   p = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(p) + 15) & ~uintptr_t(15));
@@ -1160,6 +1267,16 @@ static void run_topk_core(const uint16_t* d_db, const float* norms, uint64_t n_r
   const CUtensorMap tdb = make_map(d_db, gather_rows ? gather_rows : n_rows, BN);
   {
     ProfileScope prof(CR_KERNEL_TOPK, s);
+    if (spec_j) {
+      // Prologue launch (publish-only tiles), the speculative bound per
+      // query, then the main launch starting from it.
+      TopkParams pro = tp;
+      pro.prologue_only = 1;
+      k_topk<true><<<dim3(qtiles, slices), THREADS, SMEM_TOTAL, s>>>(tq, tdb, pro);
+      k_spec<<<div_up(n_queries, 4u), 128, 0, s>>>(tp.pub_top, 3 * n_lists, n_queries, spec_j, spec_used);
+      tp.no_prologue = 1;
+      tp.spec_used = spec_used;
+    }
     if (append) k_topk<true><<<dim3(qtiles, slices), THREADS, SMEM_TOTAL, s>>>(tq, tdb, tp);
     else k_topk<false><<<dim3(qtiles, slices), THREADS, SMEM_TOTAL, s>>>(tq, tdb, tp);
   }
@@ -1167,7 +1284,7 @@ static void run_topk_core(const uint16_t* d_db, const float* norms, uint64_t n_r
   if (append)
     merge_launch(tp.cand_s, nullptr, 0, n_queries, k, metric, 2, reinterpret_cast<const __half*>(d_queries),
                  DIM, d_out_dist, d_out_ids, s, tp.cand_cnt, cap, tp.cand_r, row_map, row_offset, tp.pub,
-                 n_lists, tp.n_rows);
+                 n_lists, tp.n_rows, spec_used, tp.err);
   else
     merge_launch(tp.part_s, tp.part_id, slices * EPI_PARTS, n_queries, k, metric, 0,
                  reinterpret_cast<const __half*>(d_queries), DIM, d_out_dist, d_out_ids, s);
@@ -1177,14 +1294,32 @@ static void run_topk_core(const uint16_t* d_db, const float* norms, uint64_t n_r
   if (tp.debug == 3) {
     uint32_t c[4];
     CR_CUDA(cudaMemcpy(c, tp.err, 16, cudaMemcpyDeviceToHost));
-    fprintf(stderr, "topk debug: lane flushes %u, warp slow paths / flush rounds %u, inserts %u\n", c[1], c[2], c[3]);
+    fprintf(stderr, "topk debug: lane flushes %u, warp slow paths / flush rounds %u, inserts %u, spec_j %u, err %u\n",
+            c[1], c[2], c[3], spec_j, c[0]);
+    if (spec_j) {
+      uint32_t sp[4];
+      float kd[4];
+      CR_CUDA(cudaMemcpy(sp, spec_used, 16, cudaMemcpyDeviceToHost));
+      for (int i = 0; i < 4; ++i)
+        CR_CUDA(cudaMemcpy(kd + i, d_out_dist + size_t(i) * k + k - 1, 4, cudaMemcpyDeviceToHost));
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t key = sp[i];
+        const uint32_t bits = key == 0 ? 0xFF800000u : ((key & 0x80000000u) ? (key & 0x7FFFFFFFu) : ~key);
+        float f;
+        memcpy(&f, &bits, 4);
+        fprintf(stderr, "  q%d spec %.5f kth %.5f\n", i, f, kd[i]);
+      }
+    }
     h_err = c[0];
   }
-  if (append && (h_err & kErrOverflow) && !(h_err & ~kErrOverflow)) {
-    // Degenerate score distribution (e.g. massive ties): redo exactly with
-    // per-list merging, which needs no candidate capacity.
+  if (append && (h_err & (kErrOverflow | kErrSpec)) && !(h_err & ~(kErrOverflow | kErrSpec))) {
+    // A candidate array overflowed (degenerate score distribution, e.g.
+    // massive ties): redo exactly with per-list merging, which needs no
+    // candidate capacity. The speculative bound was too high for some query
+    // (a sample far from the rest of the rows): redo without it.
+    const bool overflow = (h_err & kErrOverflow) != 0;
     run_topk_core(d_db, norms, n_rows, pass, row_map, d_queries, n_queries, row_offset, k, metric,
-                  d_out_dist, d_out_ids, s, false, gather_rows);
+                  d_out_dist, d_out_ids, s, !overflow, gather_rows, false);
     return;
   }
   if (h_err) fail(CR_ERR_DEVICE, "cr_filtered_topk: pipeline wait timed out (code " + std::to_string(h_err) + ")");

@@ -200,3 +200,24 @@ def test_topk_duplicate_rows_tie_break(cr, oracle, torch_, n_dup):
         assert (i[0, :m] == dup[:m]).all()
         check_topk(d.cpu().numpy(), i, d_ref, i_ref, metric)
     filt.free()
+
+
+@pytest.mark.parametrize("spec_j", ["1", "0"])
+def test_topk_speculative_bound_verified(cr, oracle, torch_, monkeypatch, spec_j):
+    """The speculative bound forced to the prologue sample's single best score
+    (above the k-th best for nearly every query): the merge must detect it and
+    the batch be redone without it. And with the bound switched off."""
+    monkeypatch.setenv("CR_TOPK_SPEC_J", spec_j)
+    n, q, k = 400_000, 200, 50
+    db, qs = make_data(n, q, seed=31)
+    rng = np.random.default_rng(32)
+    ids = np.flatnonzero(rng.random(n) < 0.2).astype(np.uint32)
+    filt = cr.upload_from_ids(ids, n)
+    words = np.zeros((n + 31) // 32, dtype=np.uint32)
+    np.bitwise_or.at(words, ids // 32, (1 << (ids % 32)).astype(np.uint32))
+    for metric in (0, 1):
+        d_ref, i_ref = oracle.topk(db, qs, k, metric, words)
+        d, i = cr.filtered_topk(torch_.from_numpy(db).cuda(), torch_.from_numpy(qs).cuda(), k, metric=metric,
+                                filter=filt)
+        check_topk(d.cpu().numpy(), i.cpu().numpy(), d_ref, i_ref, metric)
+    filt.free()
