@@ -102,6 +102,7 @@ struct TopkParams {
   // pub_top [list * 3 + i][Q]; k_spec turns their union into spec_used [Q];
   // the main launch (no_prologue) starts with that bound. The merge verifies it.
   uint32_t prologue_only;
+  uint32_t prologue_tiles;  // tiles per slice of the prologue launch
   uint32_t no_prologue;
   uint32_t* pub_top;
   const uint32_t* spec_used;
@@ -244,7 +245,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   // in publish-only mode (their best scores feed the shared bound, nothing is
   // kept), then every tile runs with the bound, those D last.
   const uint32_t T = t1 - t0;
-  const uint32_t D = (APPEND && !p.no_prologue) ? min(T, kPrologueTiles) : 0u;
+  const uint32_t D = (APPEND && !p.no_prologue) ? min(T, p.prologue_only ? p.prologue_tiles : kPrologueTiles) : 0u;
   const uint32_t n_it = p.prologue_only ? D : T + D;
   auto tile_of = [&](uint32_t it) { return it < T ? t0 + it : t0 + (it - T); };
 
@@ -501,7 +502,10 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
           for (int j = 0; j < w; ++j) t16[j] = fmaxf(t16[j], t16[j + w]);
         const float mx = t16[0];
-        const bool want = valid_q && (publish_only || mx >= bound);
+        // Publish-only tiles keep just the list's best three: the lane's own
+        // third best is its filter there.
+        const float lb = publish_only ? top3 : bound;
+        const bool want = valid_q && mx >= lb && (!publish_only || mx > top3);
         if (__any_sync(0xFFFFFFFFu, want) && p.debug != 2) {
           // Slow path, kept compact (instruction-cache friendly): the lane's
           // candidate rows as a bit mask, its 32 scores parked in shared
@@ -509,12 +513,12 @@ __global__ void __launch_bounds__(THREADS, 1)
           uint32_t c8[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};  // 8 independent OR chains
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
-            c8[j & 7] |= (v[j] >= bound ? 1u : 0u) << j;
+            c8[j & 7] |= (v[j] >= lb ? 1u : 0u) << j;
             sv[j * EPI + e_local] = v[j];
           }
           const uint32_t cm0 = (c8[0] | c8[1]) | (c8[2] | c8[3]);
           uint32_t cm = cm0 | ((c8[4] | c8[5]) | (c8[6] | c8[7]));
-          cm = want ? (publish_only ? m : (cm & m)) : 0u;
+          cm = want ? (cm & m) : 0u;
           if (APPEND && !publish_only && p.debug == 3) {
             if (cm) atomicAdd(p.err + 3, __popc(cm));
             if (lane == 0) atomicAdd(p.err + 2, 1u);
@@ -1069,6 +1073,16 @@ __global__ void __launch_bounds__(kWordTile) k_pass_compact(const uint32_t* pass
   }
 }
 
+// comp[i] = db[idx[i]] (16 lanes x 16 B per 128-dim row).
+__global__ void k_gather_rows(const uint4* db, const uint32_t* idx, uint32_t n, uint4* comp)
+{
+  const uint64_t g = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const uint64_t row = g >> 4;
+  if (row >= n) return;
+  const uint32_t src = __ldg(idx + row);
+  comp[row * 16 + (g & 15)] = __ldcs(db + uint64_t(src) * 16 + (g & 15));
+}
+
 __global__ void k_fill_empty(float* d, int64_t* ids, uint64_t n, float v)
 {
   const uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -1191,9 +1205,11 @@ static void run_topk_core(const uint16_t* d_db, const float* norms, uint64_t n_r
   // rows at or above it with probability P(Poisson(k * sample / n_rows) >=
   // spec_j) (taken below 1e-9), each list's top 3 only lowering the value.
   uint32_t spec_j = 0;
+  // Prologue launch length: up to 16 tiles per slice, at most an eighth of
+  // the slice (at least 4).
+  const uint32_t spec_tiles = std::max(kPrologueTiles, std::min(16u, tps / 8));
   if (append && allow_spec && 3 * n_lists <= 256) {
-    const uint64_t sample =
-        std::min<uint64_t>(n_rows, uint64_t(slices) * std::min<uint32_t>(tps, kPrologueTiles) * BN);
+    const uint64_t sample = std::min<uint64_t>(n_rows, uint64_t(slices) * std::min(tps, spec_tiles) * BN);
     const double f = double(sample) / double(n_rows);
     if (f <= 0.5) {
       const double lam = double(k) * f;
@@ -1272,6 +1288,7 @@ static void run_topk_core(const uint16_t* d_db, const float* norms, uint64_t n_r
       // query, then the main launch starting from it.
       TopkParams pro = tp;
       pro.prologue_only = 1;
+      pro.prologue_tiles = spec_tiles;
       k_topk<true><<<dim3(qtiles, slices), THREADS, SMEM_TOTAL, s>>>(tq, tdb, pro);
       k_spec<<<div_up(n_queries, 4u), 128, 0, s>>>(tp.pub_top, 3 * n_lists, n_queries, spec_j, spec_used);
       tp.no_prologue = 1;
@@ -1398,19 +1415,34 @@ extern "C" int cr_filtered_topk(const uint16_t* d_db, const float* d_db_norms, u
     return CR_OK;
   }
   // Pre-filter: compact the passing rows' indices (and norms) and search
-  // only those rows, fetched from the shard by TMA row gathers.
-  Scratch comp_scr(size_t(n_pass) * 4 + 256 + (l2 ? size_t(n_pass) * 4 : 0), s);
+  // only those rows: copied into a dense block first (TMA tiles), or, with
+  // CR_TOPK_GATHER=1, fetched by the producer warp from the shard directly.
+  static const bool fused_gather = getenv("CR_TOPK_GATHER") && atoi(getenv("CR_TOPK_GATHER")) == 1;
+  const size_t comp_rows = fused_gather ? 0 : n_pass;
+  Scratch comp_scr(size_t(n_pass) * 4 + 256 + (l2 ? size_t(n_pass) * 4 + 256 : 0) + comp_rows * DIM * 2, s);
   uint32_t* idx = comp_scr.as<uint32_t>();
   float* comp_norms = l2 ? reinterpret_cast<float*>(
       (reinterpret_cast<uintptr_t>(idx + n_pass) + 255) & ~uintptr_t(255)) : nullptr;
+  uint16_t* comp = reinterpret_cast<uint16_t*>(
+      (reinterpret_cast<uintptr_t>(l2 ? static_cast<void*>(comp_norms + n_pass) : static_cast<void*>(idx + n_pass)) +
+       255) & ~uintptr_t(255));
   {
     ProfileScope prof_c(CR_KERNEL_TOPK_COMPACT, s);
     k_pass_compact<<<n_wtiles, kWordTile, 0, s>>>(pass, pass_words, tiles, n_wtiles, idx, d_total,
                                                   l2 ? norms : nullptr, comp_norms);
     CR_CUDA(cudaGetLastError());
+    if (!fused_gather) {
+      k_gather_rows<<<div_up(uint64_t(n_pass) * 16, 256), 256, 0, s>>>(reinterpret_cast<const uint4*>(d_db), idx,
+                                                                      n_pass, reinterpret_cast<uint4*>(comp));
+      CR_CUDA(cudaGetLastError());
+    }
   }
-  run_topk_core(d_db, comp_norms, n_pass, nullptr, idx, d_queries, n_queries, row_offset, k, metric,
-                d_out_dist, d_out_ids, s, true, n_rows);
+  if (fused_gather)
+    run_topk_core(d_db, comp_norms, n_pass, nullptr, idx, d_queries, n_queries, row_offset, k, metric,
+                  d_out_dist, d_out_ids, s, true, n_rows);
+  else
+    run_topk_core(comp, comp_norms, n_pass, nullptr, idx, d_queries, n_queries, row_offset, k, metric,
+                  d_out_dist, d_out_ids, s);
   CR_API_END
 }
 
