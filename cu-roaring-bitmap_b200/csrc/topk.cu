@@ -471,88 +471,111 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_after();
       const uint32_t row0 = t * BN;
       const float bound = fmaxf(gthr, thr_s);
-#pragma unroll 1
-      for (uint32_t c = chalf * PART_CHUNKS; c < (p.debug == 1 ? 0u : (chalf + 1) * PART_CHUNKS); ++c) {
-        const uint32_t r0 = row0 + c * 32;
-        if (r0 >= p.n_rows) break;
-        uint32_t m = p.pass ? __ldg(p.pass + (r0 >> 5)) : 0xFFFFFFFFu;
-        const uint32_t left = p.n_rows - r0;
-        if (left < 32) m &= (1u << left) - 1u;
-        if (m == 0) continue;
-        float v[32];
-        tmem_ld32(tmem + ((quarter * 32u) << 16) + a * BN + c * 32, v);
-        if (l2) {
+      // Slow path for one 32-row chunk, kept compact (instruction-cache
+      // friendly): the lane's candidate rows as a bit mask, its 32 scores
+      // parked in shared memory, then a small loop over the set bits only.
+      auto slow = [&](const float* v, uint32_t r0, uint32_t m, float lb, bool want) {
+        uint32_t c8[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};  // 8 independent OR chains
 #pragma unroll
-          for (int j = 0; j < 32; ++j)  // rows past the mask (and n_rows) are never read
-            v[j] = ((m >> j) & 1u) ? 2.f * v[j] - __ldg(p.norms + r0 + j) : -INFINITY;
+        for (int j = 0; j < 32; ++j) {
+          c8[j & 7] |= (v[j] >= lb ? 1u : 0u) << j;
+          sv[j * EPI + e_local] = v[j];
         }
-        // Fast path: the best passing score of the chunk against the bound
-        // (a 5-level max tree, not a 32-long dependency chain).
-        float t16[16];
-        if (m == 0xFFFFFFFFu) {
-#pragma unroll
-          for (int j = 0; j < 16; ++j) t16[j] = fmaxf(v[j], v[j + 16]);
-        } else {
-#pragma unroll
-          for (int j = 0; j < 16; ++j)
-            t16[j] = fmaxf(((m >> j) & 1u) ? v[j] : -INFINITY, ((m >> (j + 16)) & 1u) ? v[j + 16] : -INFINITY);
+        const uint32_t cm0 = (c8[0] | c8[1]) | (c8[2] | c8[3]);
+        uint32_t cm = cm0 | ((c8[4] | c8[5]) | (c8[6] | c8[7]));
+        cm = want ? (cm & m) : 0u;
+        if (APPEND && !publish_only && p.debug == 3) {
+          if (cm) atomicAdd(p.err + 3, __popc(cm));
+          if (lane == 0) atomicAdd(p.err + 2, 1u);
         }
-#pragma unroll
-        for (int w = 8; w >= 1; w >>= 1)
-#pragma unroll
-          for (int j = 0; j < w; ++j) t16[j] = fmaxf(t16[j], t16[j + w]);
-        const float mx = t16[0];
-        // Publish-only tiles keep just the list's best three: the lane's own
-        // third best is its filter there.
-        const float lb = publish_only ? top3 : bound;
-        const bool want = valid_q && mx >= lb && (!publish_only || mx > top3);
-        if (__any_sync(0xFFFFFFFFu, want) && p.debug != 2) {
-          // Slow path, kept compact (instruction-cache friendly): the lane's
-          // candidate rows as a bit mask, its 32 scores parked in shared
-          // memory, then a small loop over the set bits only.
-          uint32_t c8[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};  // 8 independent OR chains
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            c8[j & 7] |= (v[j] >= lb ? 1u : 0u) << j;
-            sv[j * EPI + e_local] = v[j];
-          }
-          const uint32_t cm0 = (c8[0] | c8[1]) | (c8[2] | c8[3]);
-          uint32_t cm = cm0 | ((c8[4] | c8[5]) | (c8[6] | c8[7]));
-          cm = want ? (cm & m) : 0u;
-          if (APPEND && !publish_only && p.debug == 3) {
-            if (cm) atomicAdd(p.err + 3, __popc(cm));
-            if (lane == 0) atomicAdd(p.err + 2, 1u);
-          }
 #pragma unroll 1
-          for (uint32_t x = cm; x; x &= x - 1) {
-            const uint32_t j = __ffs(x) - 1;
-            const float val = sv[j * EPI + e_local];
-            const uint32_t r = r0 + j;
-            if (APPEND) {
-              if (!publish_only) {
-                if (nc < p.cap) {
-                  p.cand_s[cand_base + nc] = val;
-                  p.cand_r[cand_base + nc] = r;
-                }
-                ++nc;
+        for (uint32_t x = cm; x; x &= x - 1) {
+          const uint32_t j = __ffs(x) - 1;
+          const float val = sv[j * EPI + e_local];
+          const uint32_t r = r0 + j;
+          if (APPEND) {
+            if (!publish_only) {
+              if (nc < p.cap) {
+                p.cand_s[cand_base + nc] = val;
+                p.cand_r[cand_base + nc] = r;
               }
-            } else {
-              if (!(val >= gthr && better(val, r, thr_s, thr_r))) continue;
-              mybuf_s[nb] = val;
-              mybuf_r[nb] = r;
-              ++nb;
+              ++nc;
             }
-            // Re-run prologue tiles (it >= T) were already counted in the
-            // best three during the prologue; counting them again would let
-            // one row stand for two.
-            if (fast_pub && it < T && val > top3) {
-              if (val > top1) { top3 = top2; top2 = top1; top1 = val; }
-              else if (val > top2) { top3 = top2; top2 = val; }
-              else { top3 = val; }
-            }
+          } else {
+            if (!(val >= gthr && better(val, r, thr_s, thr_r))) continue;
+            mybuf_s[nb] = val;
+            mybuf_r[nb] = r;
+            ++nb;
+          }
+          // Re-run prologue tiles (it >= T) were already counted in the
+          // best three during the prologue; counting them again would let
+          // one row stand for two.
+          if (fast_pub && it < T && val > top3) {
+            if (val > top1) { top3 = top2; top2 = top1; top1 = val; }
+            else if (val > top2) { top3 = top2; top2 = val; }
+            else { top3 = val; }
           }
         }
-        if (!APPEND) flush(32);  // at most 31 + 32 entries are ever buffered
+      };
+      // Publish-only tiles keep just the list's best three: the lane's own
+      // third best is its filter there.
+      const bool whole = APPEND && !l2 && !p.pass && row0 + BN <= p.n_rows && p.debug == 0;
+      if (whole) {
+        // Every row of this part passes: one 64-column TMEM load and one
+        // 6-level max tree for the part's two chunks.
+        static_assert(PART_CHUNKS == 2, "64-column part");
+        float v[64];
+        tmem_ld64(tmem + ((quarter * 32u) << 16) + a * BN + chalf * 64, v);
+        float t[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) t[j] = fmaxf(v[j], v[j + 32]);
+#pragma unroll
+        for (int w = 16; w >= 1; w >>= 1)
+#pragma unroll
+          for (int j = 0; j < w; ++j) t[j] = fmaxf(t[j], t[j + w]);
+        const float lb = publish_only ? top3 : bound;
+        const bool want = valid_q && t[0] >= lb && (!publish_only || t[0] > top3);
+        if (__any_sync(0xFFFFFFFFu, want)) {
+          slow(v, row0 + chalf * 64, 0xFFFFFFFFu, lb, want);
+          slow(v + 32, row0 + chalf * 64 + 32, 0xFFFFFFFFu, publish_only ? top3 : bound, want);
+        }
+      } else {
+#pragma unroll 1
+        for (uint32_t c = chalf * PART_CHUNKS; c < (p.debug == 1 ? 0u : (chalf + 1) * PART_CHUNKS); ++c) {
+          const uint32_t r0 = row0 + c * 32;
+          if (r0 >= p.n_rows) break;
+          uint32_t m = p.pass ? __ldg(p.pass + (r0 >> 5)) : 0xFFFFFFFFu;
+          const uint32_t left = p.n_rows - r0;
+          if (left < 32) m &= (1u << left) - 1u;
+          if (m == 0) continue;
+          float v[32];
+          tmem_ld32(tmem + ((quarter * 32u) << 16) + a * BN + c * 32, v);
+          if (l2) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)  // rows past the mask (and n_rows) are never read
+              v[j] = ((m >> j) & 1u) ? 2.f * v[j] - __ldg(p.norms + r0 + j) : -INFINITY;
+          }
+          // Fast path: the best passing score of the chunk against the bound
+          // (a 5-level max tree, not a 32-long dependency chain).
+          float t16[16];
+          if (m == 0xFFFFFFFFu) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) t16[j] = fmaxf(v[j], v[j + 16]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              t16[j] = fmaxf(((m >> j) & 1u) ? v[j] : -INFINITY, ((m >> (j + 16)) & 1u) ? v[j + 16] : -INFINITY);
+          }
+#pragma unroll
+          for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+            for (int j = 0; j < w; ++j) t16[j] = fmaxf(t16[j], t16[j + w]);
+          const float mx = t16[0];
+          const float lb = publish_only ? top3 : bound;
+          const bool want = valid_q && mx >= lb && (!publish_only || mx > top3);
+          if (__any_sync(0xFFFFFFFFu, want) && p.debug != 2) slow(v, r0, m, lb, want);
+          if (!APPEND) flush(32);  // at most 31 + 32 entries are ever buffered
+        }
       }
       tc_fence_before();
       __syncwarp();
