@@ -77,34 +77,6 @@ __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* ba
       : "memory");
 }
 
-__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* ptr)
-{
-  uint32_t v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
-  return v;
-}
-
-// 16-byte global -> shared copy through L2 (cp.async, generic proxy).
-__device__ __forceinline__ void cp_async16(void* dst, const void* src)
-{
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-// Arrives on `bar` once all of this thread's earlier cp.async copies have
-// landed (counts as one of the barrier's expected arrivals).
-__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar)
-{
-  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
-}
-// Makes this thread's generic-proxy shared-memory writes visible to the
-// async proxy (tcgen05.mma operand reads).
-__device__ __forceinline__ void fence_proxy_async_smem()
-{
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map)
 {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

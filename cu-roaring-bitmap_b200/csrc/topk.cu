@@ -95,8 +95,6 @@ struct TopkParams {
   float* cand_s;         // [Q][n_lists][cap]
   uint32_t* cand_r;
   uint32_t* cand_cnt;    // [Q][n_lists] entries appended (may exceed cap: overflow)
-  const uint32_t* gather;   // non-null: row r of the search is gather_db row gather[r], copied
-  const uint16_t* gather_db;  // by the producer warp (cp.async) instead of a tiled TMA box
   // Speculative bound (append mode). A prologue launch (prologue_only) runs
   // the publish-only tiles and every list writes its best three scores to
   // pub_top [list * 3 + i][Q]; k_spec turns their union into spec_used [Q];
@@ -251,7 +249,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (uint32_t s = 0; s < STAGES; ++s) { mbar_init(full + s, p.gather ? 32 : 1); mbar_init(empty + s, 1); }
+    for (uint32_t s = 0; s < STAGES; ++s) { mbar_init(full + s, 1); mbar_init(empty + s, 1); }
     for (uint32_t a = 0; a < 2; ++a) { mbar_init(acc_full + a, 1); mbar_init(acc_empty + a, EPI_WARPS); }
     fence_mbar_init();
     *s_done = 0;
@@ -270,49 +268,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (warp == 0) {
     // ---------------- TMA producer
-    if (p.gather) {
-      // Whole warp: each instruction copies two 256-byte rows of the tile as
-      // 16-byte chunks into the 128-byte-swizzled K-major layout
-      // (chunk c of a 64-dim half at c ^ (row & 7)). Every lane's copies
-      // arrive on the full barrier when they land (32 arrivals); the MMA
-      // thread fences to the async proxy before reading. Rows past the last
-      // repeat a valid row; the epilogue masks them.
-      if (lane == 0) {
-        prefetch_tmap(&tq);
-        mbar_expect_tx(q_full, 2 * KB_BYTES_Q);
-        tma_load_2d(&tq, q_full, sQ, 0, int32_t(qt * BM));
-        tma_load_2d(&tq, q_full, sQ + KB_BYTES_Q, 64, int32_t(qt * BM));
-      }
-      const uint32_t last = p.n_rows - 1;
-      const uint4* gdb = reinterpret_cast<const uint4*>(p.gather_db);
-      uint32_t yn[8];
-      auto load_idx = [&](uint32_t it) {
-        const uint32_t t = tile_of(min(it, n_it - 1));
-#pragma unroll
-        for (int j = 0; j < 8; ++j) yn[j] = __ldg(p.gather + min(t * BN + lane + 32 * j, last));
-      };
-      load_idx(0);
-      for (uint32_t it = 0; it < n_it; ++it) {
-        const uint32_t s = it % STAGES;
-        uint32_t y[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) y[j] = yn[j];
-        load_idx(it + 1);
-        if (!mbar_wait(empty + s, ((it / STAGES) & 1u) ^ 1u, p.err, 1u)) break;
-        uint8_t* st = sDB + s * STAGE_BYTES;
-        // One instruction moves two whole rows: lane = (row parity, chunk).
-        const uint32_t h = lane >> 4, cc = lane & 15;
-        uint8_t* dcol = st + (cc >> 3) * KB_BYTES_DB;
-#pragma unroll
-        for (uint32_t i = 0; i < BN / 2; ++i) {
-          const uint32_t row = 2 * i + h;
-          const uint32_t src_row = __shfl_sync(0xFFFFFFFFu, y[i >> 4], row & 31);
-          cp_async16(dcol + row * 128 + (((cc & 7) ^ (row & 7)) << 4), gdb + size_t(src_row) * 16 + cc);
-        }
-        cp_async_arrive_noinc(full + s);
-      }
-      cp_async_wait<0>();
-    } else if (lane == 0) {
+    if (lane == 0) {
       prefetch_tmap(&tq);
       prefetch_tmap(&tdb);
       mbar_expect_tx(q_full, 2 * KB_BYTES_Q);
@@ -336,7 +292,6 @@ __global__ void __launch_bounds__(THREADS, 1)
         const uint32_t s = it % STAGES, a = it & 1u;
         if (!mbar_wait(full + s, (it / STAGES) & 1u, p.err, 4u)) break;
         if (!mbar_wait(acc_empty + a, ((it >> 1) & 1u) ^ 1u, p.err, 8u)) break;
-        if (p.gather) fence_proxy_async_smem();  // stage written by cp.async (generic proxy)
         tc_fence_after();
         const uint32_t adb = smem_addr(sDB + s * STAGE_BYTES);
 #pragma unroll
@@ -526,19 +481,22 @@ __global__ void __launch_bounds__(THREADS, 1)
         static_assert(PART_CHUNKS == 2, "64-column part");
         float v[64];
         tmem_ld64(tmem + ((quarter * 32u) << 16) + a * BN + chalf * 64, v);
+        // Max trees of the two 32-row halves (the slow path then runs only
+        // for a half that has a candidate in some lane).
         float t[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) t[j] = fmaxf(v[j], v[j + 32]);
+        for (int j = 0; j < 16; ++j) { t[j] = fmaxf(v[j], v[j + 16]); t[16 + j] = fmaxf(v[32 + j], v[48 + j]); }
 #pragma unroll
-        for (int w = 16; w >= 1; w >>= 1)
+        for (int w = 8; w >= 1; w >>= 1)
 #pragma unroll
-          for (int j = 0; j < w; ++j) t[j] = fmaxf(t[j], t[j + w]);
+          for (int j = 0; j < w; ++j) { t[j] = fmaxf(t[j], t[j + w]); t[16 + j] = fmaxf(t[16 + j], t[16 + j + w]); }
         const float lb = publish_only ? top3 : bound;
-        const bool want = valid_q && t[0] >= lb && (!publish_only || t[0] > top3);
-        if (__any_sync(0xFFFFFFFFu, want)) {
-          slow(v, row0 + chalf * 64, 0xFFFFFFFFu, lb, want);
-          slow(v + 32, row0 + chalf * 64 + 32, 0xFFFFFFFFu, publish_only ? top3 : bound, want);
-        }
+        const bool want0 = valid_q && t[0] >= lb && (!publish_only || t[0] > top3);
+        if (__any_sync(0xFFFFFFFFu, want0)) slow(v, row0 + chalf * 64, 0xFFFFFFFFu, lb, want0);
+        // The first half may have raised top3 (publish-only tiles).
+        const float lb1 = publish_only ? top3 : bound;
+        const bool want1 = valid_q && t[16] >= lb1 && (!publish_only || t[16] > top3);
+        if (__any_sync(0xFFFFFFFFu, want1)) slow(v + 32, row0 + chalf * 64 + 32, 0xFFFFFFFFu, lb1, want1);
       } else {
 #pragma unroll 1
         for (uint32_t c = chalf * PART_CHUNKS; c < (p.debug == 1 ? 0u : (chalf + 1) * PART_CHUNKS); ++c) {
@@ -1199,7 +1157,7 @@ static void run_topk_core(const uint16_t* d_db, const float* norms, uint64_t n_r
                           const uint32_t* row_map, const uint16_t* d_queries, uint32_t n_queries,
                           uint64_t row_offset, uint32_t k, int metric, float* d_out_dist,
                           int64_t* d_out_ids, cudaStream_t s, bool allow_append = true,
-                          uint64_t gather_rows = 0, bool allow_spec = true)
+                          bool allow_spec = true)
 {
   static std::once_flag once;
   std::call_once(once, [] {
@@ -1230,7 +1188,8 @@ static void run_topk_core(const uint16_t* d_db, const float* norms, uint64_t n_r
   uint32_t spec_j = 0;
   // Prologue launch length: up to 16 tiles per slice, at most an eighth of
   // the slice (at least 4).
-  const uint32_t spec_tiles = std::max(kPrologueTiles, std::min(16u, tps / 8));
+  uint32_t spec_tiles = std::max(kPrologueTiles, std::min(16u, tps / 8));
+  if (const char* st = getenv("CR_TOPK_SPEC_TILES")) spec_tiles = std::max(1, atoi(st));  // measurement
   if (append && allow_spec && 3 * n_lists <= 256) {
     const uint64_t sample = std::min<uint64_t>(n_rows, uint64_t(slices) * std::min(tps, spec_tiles) * BN);
     const double f = double(sample) / double(n_rows);
@@ -1299,11 +1258,7 @@ static void run_topk_core(const uint16_t* d_db, const float* norms, uint64_t n_r
   if (const char* kn = getenv("CR_TOPK_KEEPER_NS")) tp.keeper_ns = uint32_t(atoi(kn));
   CR_CUDA(cudaMemsetAsync(tp.err, 0, 16 + size_t(n_queries) * 4, s));
   const CUtensorMap tq = make_map(d_queries, n_queries, BM);
-  // Gather mode (gather_rows > 0): d_db holds gather_rows rows and search row
-  // r is d_db row row_map[r].
-  tp.gather = gather_rows ? row_map : nullptr;
-  tp.gather_db = d_db;
-  const CUtensorMap tdb = make_map(d_db, gather_rows ? gather_rows : n_rows, BN);
+  const CUtensorMap tdb = make_map(d_db, n_rows, BN);
   {
     ProfileScope prof(CR_KERNEL_TOPK, s);
     if (spec_j) {
@@ -1359,7 +1314,7 @@ static void run_topk_core(const uint16_t* d_db, const float* norms, uint64_t n_r
     // (a sample far from the rest of the rows): redo without it.
     const bool overflow = (h_err & kErrOverflow) != 0;
     run_topk_core(d_db, norms, n_rows, pass, row_map, d_queries, n_queries, row_offset, k, metric,
-                  d_out_dist, d_out_ids, s, !overflow, gather_rows, false);
+                  d_out_dist, d_out_ids, s, !overflow, false);
     return;
   }
   if (h_err) fail(CR_ERR_DEVICE, "cr_filtered_topk: pipeline wait timed out (code " + std::to_string(h_err) + ")");
@@ -1437,12 +1392,9 @@ extern "C" int cr_filtered_topk(const uint16_t* d_db, const float* d_db_norms, u
                   d_out_dist, d_out_ids, s);
     return CR_OK;
   }
-  // Pre-filter: compact the passing rows' indices (and norms) and search
-  // only those rows: copied into a dense block first (TMA tiles), or, with
-  // CR_TOPK_GATHER=1, fetched by the producer warp from the shard directly.
-  static const bool fused_gather = getenv("CR_TOPK_GATHER") && atoi(getenv("CR_TOPK_GATHER")) == 1;
-  const size_t comp_rows = fused_gather ? 0 : n_pass;
-  Scratch comp_scr(size_t(n_pass) * 4 + 256 + (l2 ? size_t(n_pass) * 4 + 256 : 0) + comp_rows * DIM * 2, s);
+  // Pre-filter: compact the passing rows' indices (and norms), copy those
+  // rows into a dense block and search it with TMA tiles.
+  Scratch comp_scr(size_t(n_pass) * 4 + 256 + (l2 ? size_t(n_pass) * 4 + 256 : 0) + size_t(n_pass) * DIM * 2, s);
   uint32_t* idx = comp_scr.as<uint32_t>();
   float* comp_norms = l2 ? reinterpret_cast<float*>(
       (reinterpret_cast<uintptr_t>(idx + n_pass) + 255) & ~uintptr_t(255)) : nullptr;
@@ -1454,18 +1406,12 @@ extern "C" int cr_filtered_topk(const uint16_t* d_db, const float* d_db_norms, u
     k_pass_compact<<<n_wtiles, kWordTile, 0, s>>>(pass, pass_words, tiles, n_wtiles, idx, d_total,
                                                   l2 ? norms : nullptr, comp_norms);
     CR_CUDA(cudaGetLastError());
-    if (!fused_gather) {
-      k_gather_rows<<<div_up(uint64_t(n_pass) * 16, 256), 256, 0, s>>>(reinterpret_cast<const uint4*>(d_db), idx,
-                                                                      n_pass, reinterpret_cast<uint4*>(comp));
-      CR_CUDA(cudaGetLastError());
-    }
+    k_gather_rows<<<div_up(uint64_t(n_pass) * 16, 256), 256, 0, s>>>(reinterpret_cast<const uint4*>(d_db), idx,
+                                                                    n_pass, reinterpret_cast<uint4*>(comp));
+    CR_CUDA(cudaGetLastError());
   }
-  if (fused_gather)
-    run_topk_core(d_db, comp_norms, n_pass, nullptr, idx, d_queries, n_queries, row_offset, k, metric,
-                  d_out_dist, d_out_ids, s, true, n_rows);
-  else
-    run_topk_core(comp, comp_norms, n_pass, nullptr, idx, d_queries, n_queries, row_offset, k, metric,
-                  d_out_dist, d_out_ids, s);
+  run_topk_core(comp, comp_norms, n_pass, nullptr, idx, d_queries, n_queries, row_offset, k, metric,
+                d_out_dist, d_out_ids, s);
   CR_API_END
 }
 

@@ -219,7 +219,7 @@ int cr_topk_merge(const float* d_dist_parts, const int64_t* d_id_parts, uint32_t
 #define CR_KERNEL_UPLOAD_EMIT 4
 #define CR_KERNEL_DECOMPRESS 5
 #define CR_KERNEL_TOPK_MERGE 6
-#define CR_KERNEL_TOPK_COMPACT 7
+#define CR_KERNEL_TOPK_COMPACT 7 /* pass-row compaction plus the row copy of the pre-filter */
 int cr_profile_enable(int on);
 int cr_profile_last_ms(int kernel, float* ms);
 
