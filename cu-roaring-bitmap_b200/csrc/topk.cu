@@ -48,7 +48,7 @@ using namespace sm100;
 constexpr uint32_t BM = 128;       // queries per CTA (UMMA M, TMEM lanes)
 constexpr uint32_t BN = 256;       // database rows per tile (UMMA N)
 constexpr uint32_t DIM = 128;      // K
-constexpr uint32_t STAGES = 2;
+constexpr uint32_t STAGES = 3;
 constexpr uint32_t EPI_WARPS = 16;  // four per TMEM lane quarter, each on a quarter of the columns
 constexpr uint32_t EPI_PARTS = EPI_WARPS / 4;          // column parts (partial lists per slice)
 constexpr uint32_t PART_CHUNKS = (BN / 32) / EPI_PARTS; // 32-row chunks per part
@@ -65,8 +65,8 @@ constexpr uint32_t SMEM_BUF_S = SMEM_DB + STAGES * STAGE_BYTES;
 constexpr uint32_t SMEM_BUF_R = SMEM_BUF_S;
 constexpr uint32_t SMEM_BAR = SMEM_BUF_R;
 constexpr uint32_t SMEM_BOUND = SMEM_BAR + 128;          // float[BM] + done counter
-constexpr uint32_t SMEM_SV = SMEM_BOUND + BM * 4 + 16;            // float[32][EPI] parked scores
-constexpr uint32_t SMEM_TOTAL = SMEM_SV + 32 * EPI * 4 + 1024;    // + alignment slack
+constexpr uint32_t SMEM_TOTAL = SMEM_BOUND + BM * 4 + 16 + 1024;  // + alignment slack
+static_assert(SMEM_TOTAL <= 232448, "shared memory per block");
 constexpr uint32_t TMEM_COLS = 512;                     // two 256-column accumulators
 constexpr uint32_t kIdesc = idesc_f16_f32(BM, BN);
 
@@ -211,6 +211,20 @@ __device__ uint32_t warp_merge_into(const float* bs, const uint32_t* br, uint32_
   return total;
 }
 
+// v[j] for a run-time j < 32 without indexing a register array (which would
+// put it in local memory): a 5-level select tree on the bits of j.
+__device__ __forceinline__ float pick32(const float* v, uint32_t j)
+{
+  float a[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) a[i] = (j & 16u) ? v[i + 16] : v[i];
+#pragma unroll
+  for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+    for (int i = 0; i < w; ++i) a[i] = (j & uint32_t(w)) ? a[i + w] : a[i];
+  return a[0];
+}
+
 template <bool APPEND>
 __global__ void __launch_bounds__(THREADS, 1)
     k_topk(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tdb,
@@ -226,14 +240,14 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint32_t* buf_r = p.buf_r + cta_id * EPI * BUF;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SMEM_BAR);
   uint64_t* q_full = bars + 0;
-  uint64_t* full = bars + 1;       // [STAGES]
-  uint64_t* empty = bars + 3;      // [STAGES]
-  uint64_t* acc_full = bars + 5;   // [2]
-  uint64_t* acc_empty = bars + 7;  // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
+  uint64_t* full = bars + 1;                   // [STAGES]
+  uint64_t* empty = bars + 1 + STAGES;         // [STAGES]
+  uint64_t* acc_full = bars + 1 + 2 * STAGES;  // [2]
+  uint64_t* acc_empty = acc_full + 2;          // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  static_assert((1 + 2 * STAGES + 4) * 8 + 8 <= 128, "barrier block");
   float* s_bound = reinterpret_cast<float*>(smem + SMEM_BOUND);
   uint32_t* s_done = reinterpret_cast<uint32_t*>(smem + SMEM_BOUND + BM * 4);
-  float* sv = reinterpret_cast<float*>(smem + SMEM_SV);
 
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t qt = blockIdx.x, slice = blockIdx.y;
@@ -427,14 +441,13 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t row0 = t * BN;
       const float bound = fmaxf(gthr, thr_s);
       // Slow path for one 32-row chunk, kept compact (instruction-cache
-      // friendly): the lane's candidate rows as a bit mask, its 32 scores
-      // parked in shared memory, then a small loop over the set bits only.
+      // friendly): the lane's candidate rows as a bit mask, then a small loop
+      // over the set bits only, each score picked from registers.
       auto slow = [&](const float* v, uint32_t r0, uint32_t m, float lb, bool want) {
         uint32_t c8[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};  // 8 independent OR chains
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           c8[j & 7] |= (v[j] >= lb ? 1u : 0u) << j;
-          sv[j * EPI + e_local] = v[j];
         }
         const uint32_t cm0 = (c8[0] | c8[1]) | (c8[2] | c8[3]);
         uint32_t cm = cm0 | ((c8[4] | c8[5]) | (c8[6] | c8[7]));
@@ -446,7 +459,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll 1
         for (uint32_t x = cm; x; x &= x - 1) {
           const uint32_t j = __ffs(x) - 1;
-          const float val = sv[j * EPI + e_local];
+          const float val = pick32(v, j);
           const uint32_t r = r0 + j;
           if (APPEND) {
             if (!publish_only) {
