@@ -208,10 +208,11 @@ DevBitmap make_dev(const cr_gpu_roaring* b, Scratch& holder, cudaStream_t s)
 namespace {
 constexpr int kProfileKinds = 8;
 bool g_profile = false;
+// Every profiled launch since cr_profile_enable(1), as (start, stop) event
+// pairs; the events are kept and reused across enables.
 struct ProfileEvents {
-  cudaEvent_t start[kProfileKinds] = {};
-  cudaEvent_t stop[kProfileKinds] = {};
-  bool used[kProfileKinds] = {};
+  std::vector<cudaEvent_t> start[kProfileKinds], stop[kProfileKinds];
+  size_t n[kProfileKinds] = {};
 };
 thread_local ProfileEvents g_prof;
 }  // namespace
@@ -219,18 +220,22 @@ thread_local ProfileEvents g_prof;
 ProfileScope::ProfileScope(int k, cudaStream_t st) : kind(k), s(st), on(g_profile)
 {
   if (!on || kind < 0 || kind >= kProfileKinds) { on = false; return; }
-  if (!g_prof.start[kind]) {
-    CR_CUDA(cudaEventCreate(&g_prof.start[kind]));
-    CR_CUDA(cudaEventCreate(&g_prof.stop[kind]));
+  const size_t i = g_prof.n[kind];
+  if (i == g_prof.start[kind].size()) {
+    cudaEvent_t a, b;
+    CR_CUDA(cudaEventCreate(&a));
+    CR_CUDA(cudaEventCreate(&b));
+    g_prof.start[kind].push_back(a);
+    g_prof.stop[kind].push_back(b);
   }
-  CR_CUDA(cudaEventRecord(g_prof.start[kind], s));
+  CR_CUDA(cudaEventRecord(g_prof.start[kind][i], s));
 }
 
 ProfileScope::~ProfileScope()
 {
   if (!on) return;
-  cudaEventRecord(g_prof.stop[kind], s);
-  g_prof.used[kind] = true;
+  cudaEventRecord(g_prof.stop[kind][g_prof.n[kind]], s);
+  ++g_prof.n[kind];
 }
 
 }  // namespace crb
@@ -239,6 +244,8 @@ using namespace crb;
 
 extern "C" int cr_profile_enable(int on)
 {
+  if (on && !g_profile)
+    for (int k = 0; k < kProfileKinds; ++k) g_prof.n[k] = 0;
   g_profile = on != 0;
   return CR_OK;
 }
@@ -247,9 +254,28 @@ extern "C" int cr_profile_last_ms(int kernel, float* ms)
 {
   CR_API_BEGIN
   CR_REQUIRE(ms != nullptr && kernel >= 0 && kernel < kProfileKinds, "cr_profile_last_ms: bad argument");
-  CR_REQUIRE(g_prof.used[kernel], "cr_profile_last_ms: no profiled launch of this kernel");
-  CR_CUDA(cudaEventSynchronize(g_prof.stop[kernel]));
-  CR_CUDA(cudaEventElapsedTime(ms, g_prof.start[kernel], g_prof.stop[kernel]));
+  const size_t n = g_prof.n[kernel];
+  CR_REQUIRE(n > 0, "cr_profile_last_ms: no profiled launch of this kernel");
+  CR_CUDA(cudaEventSynchronize(g_prof.stop[kernel][n - 1]));
+  CR_CUDA(cudaEventElapsedTime(ms, g_prof.start[kernel][n - 1], g_prof.stop[kernel][n - 1]));
+  CR_API_END
+}
+
+extern "C" int cr_profile_sum_ms(int kernel, float* total_ms, uint32_t* count)
+{
+  CR_API_BEGIN
+  CR_REQUIRE(total_ms != nullptr && count != nullptr && kernel >= 0 && kernel < kProfileKinds,
+             "cr_profile_sum_ms: bad argument");
+  const size_t n = g_prof.n[kernel];
+  double sum = 0.0;
+  for (size_t i = 0; i < n; ++i) {
+    float ms = 0.f;
+    CR_CUDA(cudaEventSynchronize(g_prof.stop[kernel][i]));
+    CR_CUDA(cudaEventElapsedTime(&ms, g_prof.start[kernel][i], g_prof.stop[kernel][i]));
+    sum += ms;
+  }
+  *total_ms = float(sum);
+  *count = uint32_t(n);
   CR_API_END
 }
 

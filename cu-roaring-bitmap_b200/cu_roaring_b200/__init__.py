@@ -35,7 +35,7 @@ EXPORTED_SYMBOLS = (
     "cr_promote_auto", "cr_deep_copy", "cr_set_operation", "cr_multi_and", "cr_multi_or",
     "cr_decompress_to_bitset", "cr_decompress_to_bitset_alloc", "cr_enumerate_ids_i64",
     "cr_enumerate_ids_u32", "cr_enumerate_ids_alloc", "cr_enumerate_ids_u32_noalloc", "cr_contains_batch", "cr_filtered_topk",
-    "cr_row_norms", "cr_topk_merge", "cr_profile_enable", "cr_profile_last_ms",
+    "cr_row_norms", "cr_topk_merge", "cr_profile_enable", "cr_profile_last_ms", "cr_profile_sum_ms",
 )
 
 
@@ -85,6 +85,7 @@ _sigs = {
     "cr_topk_merge": ([_vp, _vp, _u32, _u32, _u32, _i32, _vp, _vp, _vp], _i32),
     "cr_profile_enable": ([_i32], _i32),
     "cr_profile_last_ms": ([_i32, C.POINTER(C.c_float)], _i32),
+    "cr_profile_sum_ms": ([_i32, C.POINTER(C.c_float), C.POINTER(C.c_uint32)], _i32),
 }
 for _name, (_args, _res) in _sigs.items():
     _f = getattr(_lib, _name)
@@ -387,6 +388,14 @@ def topk_merge(dist_parts, id_parts, k: int, metric: int = METRIC_IP, stream=Non
 
 def profile_enable(on: bool = True) -> None:
     _lib.cr_profile_enable(int(on))
+
+
+def profile_mean_ms(kernel: int) -> tuple[float, int]:
+    """Mean device time of the profiled launches of `kernel` since profiling
+    was switched on, and their number (0.0, 0 when none)."""
+    tot, n = C.c_float(), C.c_uint32()
+    _check(_lib.cr_profile_sum_ms(kernel, C.byref(tot), C.byref(n)), "profile_sum_ms")
+    return (tot.value / n.value if n.value else 0.0), n.value
 
 
 def profile_last_ms(kernel: int) -> float:

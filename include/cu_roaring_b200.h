@@ -222,6 +222,9 @@ int cr_topk_merge(const float* d_dist_parts, const int64_t* d_id_parts, uint32_t
 #define CR_KERNEL_TOPK_COMPACT 7 /* pass-row compaction plus the row copy of the pre-filter */
 int cr_profile_enable(int on);
 int cr_profile_last_ms(int kernel, float* ms);
+/* Sum of the device times of every profiled launch of `kernel` since
+ * profiling was last switched on, and their number (waits for them). */
+int cr_profile_sum_ms(int kernel, float* total_ms, uint32_t* count);
 
 #ifdef __cplusplus
 }
