@@ -485,8 +485,16 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
         }
       };
-      // Publish-only tiles keep just the list's best three: the lane's own
-      // third best is its filter there.
+      // Publish-only tiles keep just the list's best three, fed with the
+      // maximum of every 32-row chunk (real scores of distinct rows, so each
+      // list still holds three rows at or above them).
+      auto take_top = [&](float x) {
+        if (x > top3) {
+          if (x > top1) { top3 = top2; top2 = top1; top1 = x; }
+          else if (x > top2) { top3 = top2; top2 = x; }
+          else { top3 = x; }
+        }
+      };
       const bool whole = APPEND && !l2 && !p.pass && row0 + BN <= p.n_rows && p.debug == 0;
       if (whole) {
         // Every row of this part passes: one 64-column TMEM load and one
@@ -503,13 +511,14 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int w = 8; w >= 1; w >>= 1)
 #pragma unroll
           for (int j = 0; j < w; ++j) { t[j] = fmaxf(t[j], t[j + w]); t[16 + j] = fmaxf(t[16 + j], t[16 + j + w]); }
-        const float lb = publish_only ? top3 : bound;
-        const bool want0 = valid_q && t[0] >= lb && (!publish_only || t[0] > top3);
-        if (__any_sync(0xFFFFFFFFu, want0)) slow(v, row0 + chalf * 64, 0xFFFFFFFFu, lb, want0);
-        // The first half may have raised top3 (publish-only tiles).
-        const float lb1 = publish_only ? top3 : bound;
-        const bool want1 = valid_q && t[16] >= lb1 && (!publish_only || t[16] > top3);
-        if (__any_sync(0xFFFFFFFFu, want1)) slow(v + 32, row0 + chalf * 64 + 32, 0xFFFFFFFFu, lb1, want1);
+        if (publish_only) {
+          if (valid_q) { take_top(t[0]); take_top(t[16]); }
+        } else {
+          const bool want0 = valid_q && t[0] >= bound;
+          if (__any_sync(0xFFFFFFFFu, want0)) slow(v, row0 + chalf * 64, 0xFFFFFFFFu, bound, want0);
+          const bool want1 = valid_q && t[16] >= bound;
+          if (__any_sync(0xFFFFFFFFu, want1)) slow(v + 32, row0 + chalf * 64 + 32, 0xFFFFFFFFu, bound, want1);
+        }
       } else {
 #pragma unroll 1
         for (uint32_t c = chalf * PART_CHUNKS; c < (p.debug == 1 ? 0u : (chalf + 1) * PART_CHUNKS); ++c) {
@@ -542,9 +551,12 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
             for (int j = 0; j < w; ++j) t16[j] = fmaxf(t16[j], t16[j + w]);
           const float mx = t16[0];
-          const float lb = publish_only ? top3 : bound;
-          const bool want = valid_q && mx >= lb && (!publish_only || mx > top3);
-          if (__any_sync(0xFFFFFFFFu, want) && p.debug != 2) slow(v, r0, m, lb, want);
+          if (publish_only) {
+            if (valid_q) take_top(mx);
+          } else {
+            const bool want = valid_q && mx >= bound;
+            if (__any_sync(0xFFFFFFFFu, want) && p.debug != 2) slow(v, r0, m, bound, want);
+          }
           if (!APPEND) flush(32);  // at most 31 + 32 entries are ever buffered
         }
       }
@@ -1027,13 +1039,16 @@ __global__ void k_row_norms(const uint4* db, uint64_t n_rows, float* out)
 constexpr uint32_t kWordTile = 1024;
 
 __global__ void __launch_bounds__(kWordTile) k_pass_tile_sums(const uint32_t* pass, uint64_t n_words,
-                                                              uint32_t* tile_sums)
+                                                              uint32_t* tile_sums, uint32_t* total)
 {
   __shared__ uint32_t s_red[32];
   const uint64_t w = uint64_t(blockIdx.x) * kWordTile + threadIdx.x;
   const uint32_t c = w < n_words ? __popc(pass[w]) : 0u;
   const uint32_t t = block_sum<kWordTile>(c, s_red);
-  if (threadIdx.x == 0) tile_sums[blockIdx.x] = t;
+  if (threadIdx.x == 0) {
+    tile_sums[blockIdx.x] = t;
+    atomicAdd(total, t);
+  }
 }
 
 // idx[] = shard rows whose filter bit is set, ascending; *total = count.
@@ -1164,6 +1179,49 @@ extern "C" int cr_row_norms(const uint16_t* d_db, uint64_t n_rows, uint32_t dim,
   CR_API_END
 }
 
+// Measurement only (CR_TOPK_TRACE=1): events at the phase boundaries of one
+// call, printed as the device time between consecutive marks.
+struct Trace {
+  bool on = false;
+  cudaEvent_t ev[16];
+  const char* name[16];
+  int n = 0;
+  static Trace& get()
+  {
+    thread_local Trace t;
+    return t;
+  }
+  void mark(const char* what, cudaStream_t s)
+  {
+    if (!on || n >= 16) return;
+    if (!ev[n]) cudaEventCreate(&ev[n]);
+    name[n] = what;
+    cudaEventRecord(ev[n++], s);
+  }
+  void print()
+  {
+    if (!on || n < 2) return;
+    cudaEventSynchronize(ev[n - 1]);
+    fprintf(stderr, "topk trace:");
+    for (int i = 1; i < n; ++i) {
+      float ms = 0.f;
+      cudaEventElapsedTime(&ms, ev[i - 1], ev[i]);
+      fprintf(stderr, " %s %.1f", name[i], ms * 1e3f);
+    }
+    fprintf(stderr, " (us)\n");
+  }
+  Trace() { for (auto& e : ev) e = nullptr; }
+};
+
+// A small page-locked host buffer per thread for the counts the host reads
+// back (a pageable destination makes the copy slower).
+static uint32_t* pinned_words()
+{
+  thread_local uint32_t* buf = nullptr;
+  if (!buf) CR_CUDA(cudaMallocHost(reinterpret_cast<void**>(&buf), 64));
+  return buf;
+}
+
 // The tcgen05 search over `n_rows` rows (optionally masked by `pass`, row
 // ids optionally translated by `row_map`) plus the per-query merge.
 static void run_topk_core(const uint16_t* d_db, const float* norms, uint64_t n_rows, const uint32_t* pass,
@@ -1226,9 +1284,21 @@ static void run_topk_core(const uint16_t* d_db, const float* norms, uint64_t n_r
   }
   const size_t spec_b = spec_j ? size_t(n_queries) * n_lists * 3 * 4 + size_t(n_queries) * 4 + 16 : 0;
   Scratch scr(list_b * 2 + cbuf_b * 2 + part_b * 12 + pub_b + cand_b * 2 + size_t(n_queries) * n_lists * 4 +
-                  size_t(n_queries) * 8 + 64 + 512 + spec_b, s);
+                  size_t(n_queries) * 8 + 64 + 512 + spec_b + 256, s);
   char* p = scr.as<char>();
   TopkParams tp{};
+  // Everything that must start at zero sits in one block at the front, cleared
+  // by one memset: error word + counters, per-query shared thresholds,
+  // published bounds, candidate counts, published best three.
+  const size_t zero_b = 16 + size_t(n_queries) * 4 + pub_b + (append ? size_t(n_queries) * n_lists * 4 : 0) +
+                        (spec_j ? size_t(n_queries) * n_lists * 3 * 4 : 0);
+  tp.err = reinterpret_cast<uint32_t*>(p); p += 16;
+  tp.shared_thr = reinterpret_cast<uint32_t*>(p); p += size_t(n_queries) * 4;
+  tp.pub = reinterpret_cast<uint32_t*>(p); p += pub_b;
+  if (append) { tp.cand_cnt = reinterpret_cast<uint32_t*>(p); p += size_t(n_queries) * n_lists * 4; }
+  if (spec_j) { tp.pub_top = reinterpret_cast<uint32_t*>(p); p += size_t(n_queries) * n_lists * 3 * 4; }
+  CR_CUDA(cudaMemsetAsync(tp.err, 0, zero_b, s));
+  p = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(p) + 255) & ~uintptr_t(255));
   tp.n_rows = static_cast<uint32_t>(n_rows);
   tp.n_queries = n_queries;
   tp.k = k;
@@ -1243,33 +1313,24 @@ static void run_topk_core(const uint16_t* d_db, const float* norms, uint64_t n_r
   tp.list_r = reinterpret_cast<uint32_t*>(p); p += list_b;
   tp.buf_s = reinterpret_cast<float*>(p); p += cbuf_b;
   tp.buf_r = reinterpret_cast<uint32_t*>(p); p += cbuf_b;
-  tp.pub = reinterpret_cast<uint32_t*>(p); p += pub_b;
   tp.n_lists = n_lists;
   tp.jth = jth;
-  CR_CUDA(cudaMemsetAsync(tp.pub, 0, pub_b, s));
   tp.append = append ? 1u : 0u;
   tp.cap = cap;
   if (append) {
     tp.cand_s = reinterpret_cast<float*>(p); p += cand_b;
     tp.cand_r = reinterpret_cast<uint32_t*>(p); p += cand_b;
-    tp.cand_cnt = reinterpret_cast<uint32_t*>(p); p += size_t(n_queries) * n_lists * 4;
-    CR_CUDA(cudaMemsetAsync(tp.cand_cnt, 0, size_t(n_queries) * n_lists * 4, s));
   }
   uint32_t* spec_used = nullptr;
   if (spec_j) {
-    tp.pub_top = reinterpret_cast<uint32_t*>(p); p += size_t(n_queries) * n_lists * 3 * 4;
     spec_used = reinterpret_cast<uint32_t*>(p); p += size_t(n_queries) * 4 + 16;
-    CR_CUDA(cudaMemsetAsync(tp.pub_top, 0, size_t(n_queries) * n_lists * 3 * 4, s));
   }
   tp.part_id = reinterpret_cast<int64_t*>(p); p += part_b * 8;
   tp.part_s = reinterpret_cast<float*>(p); p += part_b * 4;
-  p = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(p) + 15) & ~uintptr_t(15));
-  tp.err = reinterpret_cast<uint32_t*>(p);
-  tp.shared_thr = tp.err + 4;
   if (const char* dbg = getenv("CR_TOPK_DEBUG")) tp.debug = uint32_t(atoi(dbg));
   tp.keeper_ns = 2000;
   if (const char* kn = getenv("CR_TOPK_KEEPER_NS")) tp.keeper_ns = uint32_t(atoi(kn));
-  CR_CUDA(cudaMemsetAsync(tp.err, 0, 16 + size_t(n_queries) * 4, s));
+  Trace::get().mark("setup", s);
   const CUtensorMap tq = make_map(d_queries, n_queries, BM);
   const CUtensorMap tdb = make_map(d_db, n_rows, BN);
   {
@@ -1285,6 +1346,7 @@ static void run_topk_core(const uint16_t* d_db, const float* norms, uint64_t n_r
       tp.no_prologue = 1;
       tp.spec_used = spec_used;
     }
+    Trace::get().mark("prologue_spec", s);
     if (append) k_topk<true><<<dim3(qtiles, slices), THREADS, SMEM_TOTAL, s>>>(tq, tdb, tp);
     else k_topk<false><<<dim3(qtiles, slices), THREADS, SMEM_TOTAL, s>>>(tq, tdb, tp);
   }
@@ -1296,9 +1358,11 @@ static void run_topk_core(const uint16_t* d_db, const float* norms, uint64_t n_r
   else
     merge_launch(tp.part_s, tp.part_id, slices * EPI_PARTS, n_queries, k, metric, 0,
                  reinterpret_cast<const __half*>(d_queries), DIM, d_out_dist, d_out_ids, s);
-  uint32_t h_err = 0;
-  CR_CUDA(cudaMemcpyAsync(&h_err, tp.err, 4, cudaMemcpyDeviceToHost, s));
+  Trace::get().mark("main_merge", s);
+  uint32_t* h_word = pinned_words();
+  CR_CUDA(cudaMemcpyAsync(h_word, tp.err, 4, cudaMemcpyDeviceToHost, s));
   CR_CUDA(cudaStreamSynchronize(s));
+  uint32_t h_err = h_word[0];
   if (tp.debug == 3) {
     uint32_t c[4];
     CR_CUDA(cudaMemcpy(c, tp.err, 16, cudaMemcpyDeviceToHost));
@@ -1351,6 +1415,10 @@ extern "C" int cr_filtered_topk(const uint16_t* d_db, const float* d_db_norms, u
              "cr_filtered_topk: db and queries must be 16-byte aligned");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const bool l2 = metric == CR_METRIC_L2;
+  Trace& tr = Trace::get();
+  tr.on = getenv("CR_TOPK_TRACE") != nullptr;
+  tr.n = 0;
+  tr.mark("start", s);
 
   // Squared norms of the shard rows (L2 only), computed here when not given.
   Scratch norm_scr((l2 && !d_db_norms) ? n_rows * 4 : 0, s);
@@ -1382,17 +1450,15 @@ extern "C" int cr_filtered_topk(const uint16_t* d_db, const float* d_db_norms, u
     const int grid = static_cast<int>(std::min<uint64_t>(div_up(threads, 256), uint64_t(sm_count()) * 16));
     k_pass_bits<<<grid, 256, 0, s>>>(v, row_offset, n_rows, pass, pass_words, filter->universe_size);
   }
-  k_pass_tile_sums<<<n_wtiles, kWordTile, 0, s>>>(pass, pass_words, tiles);
+  CR_CUDA(cudaMemsetAsync(d_total + 1, 0, 4, s));
+  k_pass_tile_sums<<<n_wtiles, kWordTile, 0, s>>>(pass, pass_words, tiles, d_total + 1);
   CR_CUDA(cudaGetLastError());
   // Count first: the compacted copy is only worth it below half density.
-  uint32_t h_tiles_total = 0;
-  {
-    std::vector<uint32_t> h(n_wtiles);
-    CR_CUDA(cudaMemcpyAsync(h.data(), tiles, n_wtiles * 4, cudaMemcpyDeviceToHost, s));
-    CR_CUDA(cudaStreamSynchronize(s));
-    for (uint32_t x : h) h_tiles_total += x;
-  }
-  const uint32_t n_pass = h_tiles_total;
+  tr.mark("pass_bits", s);
+  uint32_t* h_word = pinned_words();
+  CR_CUDA(cudaMemcpyAsync(h_word, d_total + 1, 4, cudaMemcpyDeviceToHost, s));
+  CR_CUDA(cudaStreamSynchronize(s));
+  const uint32_t n_pass = h_word[0];
   if (n_pass == 0) {
     const uint64_t n = uint64_t(n_queries) * k;
     k_fill_empty<<<div_up(n, 256), 256, 0, s>>>(d_out_dist, d_out_ids, n, l2 ? INFINITY : -INFINITY);
@@ -1415,6 +1481,7 @@ extern "C" int cr_filtered_topk(const uint16_t* d_db, const float* d_db_norms, u
       (reinterpret_cast<uintptr_t>(l2 ? static_cast<void*>(comp_norms + n_pass) : static_cast<void*>(idx + n_pass)) +
        255) & ~uintptr_t(255));
   {
+    tr.mark("count_sync", s);
     ProfileScope prof_c(CR_KERNEL_TOPK_COMPACT, s);
     k_pass_compact<<<n_wtiles, kWordTile, 0, s>>>(pass, pass_words, tiles, n_wtiles, idx, d_total,
                                                   l2 ? norms : nullptr, comp_norms);
@@ -1423,8 +1490,11 @@ extern "C" int cr_filtered_topk(const uint16_t* d_db, const float* d_db_norms, u
                                                                     n_pass, reinterpret_cast<uint4*>(comp));
     CR_CUDA(cudaGetLastError());
   }
+  tr.mark("compact_gather", s);
   run_topk_core(comp, comp_norms, n_pass, nullptr, idx, d_queries, n_queries, row_offset, k, metric,
                 d_out_dist, d_out_ids, s);
+  tr.mark("search", s);
+  tr.print();
   CR_API_END
 }
 
