@@ -582,7 +582,7 @@ def main():
                          "frac": achieved / peak, "traffic": None,
                          "kernel": "k_topk", "kernel_ms": kern_ms,
                          "other_kernels_ms": {"k_merge": float(np.mean(merge_ms)) if merge_ms else None,
-                                              "k_pass_compact+k_gather_rows": float(np.mean(gather_ms)) if gather_ms else None},
+                                              "k_pass_compact": float(np.mean(gather_ms)) if gather_ms else None},
                          "algorithmic": "2*Q*rows_searched*128 flops per launch",
                          "rows_searched": rows_searched,
                          "dense_equivalent_tflops": 2.0 * N_QUERIES * rows_local * DIM / (kern_ms / 1e3) / 1e12,

@@ -1052,27 +1052,30 @@ __global__ void __launch_bounds__(kWordTile) k_pass_tile_sums(const uint32_t* pa
 }
 
 // idx[] = shard rows whose filter bit is set, ascending; *total = count.
+// With `comp`, the block then copies its rows: comp[i] = db[idx[i]]
+// (16 threads x 16 B per 128-dim row), so the gather needs no launch of its
+// own and starts as soon as the block's indices are known.
 __global__ void __launch_bounds__(kWordTile) k_pass_compact(const uint32_t* pass, uint64_t n_words,
                                                             const uint32_t* tile_sums, uint32_t n_tiles,
                                                             uint32_t* idx, uint32_t* total,
-                                                            const float* norms, float* comp_norms)
+                                                            const float* norms, float* comp_norms,
+                                                            const uint4* db, uint4* comp)
 {
   __shared__ uint32_t s_red[32];
-  __shared__ uint32_t s_base;
-  if (threadIdx.x == 0) {
-    uint32_t b = 0, all = 0;
-    for (uint32_t j = 0; j < n_tiles; ++j) {
-      if (j < blockIdx.x) b += tile_sums[j];
-      all += tile_sums[j];
-    }
-    s_base = b;
-    if (blockIdx.x == 0) *total = all;
+  // Rows of the earlier word tiles: the block's first output slot.
+  uint32_t before = 0, all = 0;
+  for (uint32_t j = threadIdx.x; j < n_tiles; j += kWordTile) {
+    const uint32_t c = tile_sums[j];
+    if (j < blockIdx.x) before += c;
+    all += c;
   }
-  __syncthreads();
+  const uint32_t base = block_sum<kWordTile>(before, s_red);
+  const uint32_t everything = block_sum<kWordTile>(all, s_red);
+  if (blockIdx.x == 0 && threadIdx.x == 0) *total = everything;
   const uint64_t w = uint64_t(blockIdx.x) * kWordTile + threadIdx.x;
   uint32_t x = w < n_words ? pass[w] : 0u;
   uint32_t tot;
-  uint32_t pos = s_base + block_exclusive_scan<kWordTile>(uint32_t(__popc(x)), s_red, &tot);
+  uint32_t pos = base + block_exclusive_scan<kWordTile>(uint32_t(__popc(x)), s_red, &tot);
   while (x) {
     const uint32_t r = uint32_t(w * 32 + __ffs(x) - 1);
     idx[pos] = r;
@@ -1080,16 +1083,23 @@ __global__ void __launch_bounds__(kWordTile) k_pass_compact(const uint32_t* pass
     ++pos;
     x &= x - 1;
   }
-}
-
-// comp[i] = db[idx[i]] (16 lanes x 16 B per 128-dim row).
-__global__ void k_gather_rows(const uint4* db, const uint32_t* idx, uint32_t n, uint4* comp)
-{
-  const uint64_t g = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  const uint64_t row = g >> 4;
-  if (row >= n) return;
-  const uint32_t src = __ldg(idx + row);
-  comp[row * 16 + (g & 15)] = __ldcs(db + uint64_t(src) * 16 + (g & 15));
+  if (!comp) return;
+  __syncthreads();  // the block's idx[] entries are visible to all its threads
+  const uint32_t n16 = tot * 16;
+  constexpr uint32_t U = 4;  // independent row loads in flight per thread
+  for (uint32_t i0 = 0; i0 < n16; i0 += kWordTile * U) {
+    uint4 v[U];
+    uint32_t dst[U];
+#pragma unroll
+    for (uint32_t u = 0; u < U; ++u) {
+      const uint32_t i = i0 + u * kWordTile + threadIdx.x;
+      dst[u] = i < n16 ? base * 16 + i : 0xFFFFFFFFu;
+      if (i < n16) v[u] = __ldcs(db + uint64_t(idx[base + i / 16]) * 16 + (i & 15));
+    }
+#pragma unroll
+    for (uint32_t u = 0; u < U; ++u)
+      if (dst[u] != 0xFFFFFFFFu) comp[size_t(dst[u])] = v[u];
+  }
 }
 
 __global__ void k_fill_empty(float* d, int64_t* ids, uint64_t n, float v)
@@ -1484,10 +1494,8 @@ extern "C" int cr_filtered_topk(const uint16_t* d_db, const float* d_db_norms, u
     tr.mark("count_sync", s);
     ProfileScope prof_c(CR_KERNEL_TOPK_COMPACT, s);
     k_pass_compact<<<n_wtiles, kWordTile, 0, s>>>(pass, pass_words, tiles, n_wtiles, idx, d_total,
-                                                  l2 ? norms : nullptr, comp_norms);
-    CR_CUDA(cudaGetLastError());
-    k_gather_rows<<<div_up(uint64_t(n_pass) * 16, 256), 256, 0, s>>>(reinterpret_cast<const uint4*>(d_db), idx,
-                                                                    n_pass, reinterpret_cast<uint4*>(comp));
+                                                  l2 ? norms : nullptr, comp_norms,
+                                                  reinterpret_cast<const uint4*>(d_db), reinterpret_cast<uint4*>(comp));
     CR_CUDA(cudaGetLastError());
   }
   tr.mark("compact_gather", s);
