@@ -1267,9 +1267,9 @@ static void run_topk_core(const uint16_t* d_db, const float* norms, uint64_t n_r
   // rows at or above it with probability P(Poisson(k * sample / n_rows) >=
   // spec_j) (taken below 1e-9), each list's top 3 only lowering the value.
   uint32_t spec_j = 0;
-  // Prologue launch length: up to 16 tiles per slice, at most an eighth of
+  // Prologue launch length: up to 24 tiles per slice, at most an eighth of
   // the slice (at least 4).
-  uint32_t spec_tiles = std::max(kPrologueTiles, std::min(16u, tps / 8));
+  uint32_t spec_tiles = std::max(kPrologueTiles, std::min(24u, tps / 8));
   if (const char* st = getenv("CR_TOPK_SPEC_TILES")) spec_tiles = std::max(1, atoi(st));  // measurement
   if (append && allow_spec && 3 * n_lists <= 256) {
     const uint64_t sample = std::min<uint64_t>(n_rows, uint64_t(slices) * std::min(tps, spec_tiles) * BN);
