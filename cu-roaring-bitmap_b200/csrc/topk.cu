@@ -743,6 +743,102 @@ __global__ void __launch_bounds__(MERGE_THREADS) k_merge(const float* part_s, co
     s[slot] = v;
     id[slot] = i;
   };
+  // Best k of the n entries in s/id [0, n) (n <= MERGE_N - kSelMax), written
+  // to the outputs: radix select of the k-th best score key, then an exact
+  // rank (score desc, id asc) of the entries at or above it. False (nothing
+  // written) when more than kSelMax entries tie at or above that key.
+  constexpr uint32_t kSelMax = MERGE_THREADS;  // selected set ranked one per thread
+  __shared__ uint32_t s_hist[256];
+  __shared__ uint32_t s_sel[3];
+  __shared__ uint32_t s_m;
+  auto dist_of = [&](float x, int64_t r) {
+    if (r < 0) return l2 ? INFINITY : -INFINITY;
+    if (!l2) return x;
+    return kind != 1 ? s_qn - x : -x;
+  };
+  auto select_out = [&](uint32_t n) -> bool {
+    // Radix select (8-bit digits, most significant first) of the k-th best
+    // score key T; the selected set is every survivor with key >= T.
+    uint32_t thr = 0;
+    if (n > k) {
+      uint32_t prefix = 0, mask = 0, rem = k;
+      for (int shift = 24; shift >= 0; shift -= 8) {
+        for (uint32_t b = threadIdx.x; b < 256; b += MERGE_THREADS) s_hist[b] = 0;
+        __syncthreads();
+        for (uint32_t e = threadIdx.x; e < n; e += MERGE_THREADS) {
+          const uint32_t key = score_key(s[e]);
+          if ((key & mask) == prefix) atomicAdd(&s_hist[(key >> shift) & 255u], 1u);
+        }
+        __syncthreads();
+        if (threadIdx.x < 32) {
+          const uint32_t lane = threadIdx.x;
+          uint32_t cnt[8], tot = 0;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) { cnt[j] = s_hist[255 - (8 * lane + j)]; tot += cnt[j]; }
+          uint32_t x = tot;
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, x, o);
+            if (lane >= o) x += y;
+          }
+          const uint32_t before = x - tot;  // survivors in higher digits
+          if (before < rem && rem <= x) {
+            uint32_t acc = before;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              if (acc + cnt[j] >= rem) {
+                s_sel[0] = prefix | (uint32_t(255 - (8 * lane + j)) << shift);
+                s_sel[1] = rem - acc;
+                break;
+              }
+              acc += cnt[j];
+            }
+          }
+        }
+        __syncthreads();
+        prefix = s_sel[0];
+        rem = s_sel[1];
+        mask |= 255u << shift;
+      }
+      thr = prefix;
+      if (threadIdx.x == 0 && thr < spec) atomicOr(err, kErrSpec);
+    } else if (threadIdx.x == 0 && spec && !s_over) {
+      atomicOr(err, kErrSpec);  // fewer than k kept: the bound may have dropped some
+    }
+    // Compact key >= T into the tail slots.
+    if (threadIdx.x == 0) s_m = 0;
+    __syncthreads();
+    float* cs = s + (MERGE_N - kSelMax);
+    int64_t* cid = id + (MERGE_N - kSelMax);
+    for (uint32_t e = threadIdx.x; e < n; e += MERGE_THREADS) {
+      if (score_key(s[e]) >= thr) {
+        const uint32_t slot = atomicAdd(&s_m, 1u);
+        if (slot < kSelMax) { cs[slot] = s[e]; cid[slot] = id[e]; }
+      }
+    }
+    __syncthreads();
+    const uint32_t m = s_m;
+    if (m <= kSelMax) {
+      // Exact rank of each selected entry (score desc, id asc); the best k
+      // go straight to their output slots.
+      if (threadIdx.x < m) {
+        const float x = cs[threadIdx.x];
+        const int64_t g = cid[threadIdx.x];
+        uint32_t rank = 0;
+        for (uint32_t j = 0; j < m; ++j) rank += better64(cs[j], cid[j], x, g) ? 1u : 0u;
+        if (rank < k) {
+          out_d[size_t(q) * k + rank] = dist_of(x, g);
+          out_id[size_t(q) * k + rank] = g;
+        }
+      }
+      for (uint32_t i = m + threadIdx.x; i < k; i += MERGE_THREADS) {
+        out_d[size_t(q) * k + i] = l2 ? INFINITY : -INFINITY;
+        out_id[size_t(q) * k + i] = -1;
+      }
+      return true;
+    }
+    return false;
+  };
   if (kind == 2) {
     // Per-list counts -> prefix in shared memory (flattened candidate index
     // -> (list, entry)).
@@ -794,93 +890,7 @@ __global__ void __launch_bounds__(MERGE_THREADS) k_merge(const float* part_s, co
     __syncthreads();
     const uint32_t n = s_fill;
     __syncthreads();  // every thread has n before the fallback below resets s_fill
-    constexpr uint32_t kSelMax = MERGE_THREADS;  // selected set ranked one per thread
-    if (n <= MERGE_N - kSelMax) {
-      // Radix select (8-bit digits, most significant first) of the k-th best
-      // score key T; the selected set is every survivor with key >= T.
-      __shared__ uint32_t s_hist[256];
-      __shared__ uint32_t s_sel[3];
-      uint32_t thr = 0;
-      if (n > k) {
-        uint32_t prefix = 0, mask = 0, rem = k;
-        for (int shift = 24; shift >= 0; shift -= 8) {
-          for (uint32_t b = threadIdx.x; b < 256; b += MERGE_THREADS) s_hist[b] = 0;
-          __syncthreads();
-          for (uint32_t e = threadIdx.x; e < n; e += MERGE_THREADS) {
-            const uint32_t key = score_key(s[e]);
-            if ((key & mask) == prefix) atomicAdd(&s_hist[(key >> shift) & 255u], 1u);
-          }
-          __syncthreads();
-          if (threadIdx.x < 32) {
-            const uint32_t lane = threadIdx.x;
-            uint32_t cnt[8], tot = 0;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) { cnt[j] = s_hist[255 - (8 * lane + j)]; tot += cnt[j]; }
-            uint32_t x = tot;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-              const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, x, o);
-              if (lane >= o) x += y;
-            }
-            const uint32_t before = x - tot;  // survivors in higher digits
-            if (before < rem && rem <= x) {
-              uint32_t acc = before;
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                if (acc + cnt[j] >= rem) {
-                  s_sel[0] = prefix | (uint32_t(255 - (8 * lane + j)) << shift);
-                  s_sel[1] = rem - acc;
-                  break;
-                }
-                acc += cnt[j];
-              }
-            }
-          }
-          __syncthreads();
-          prefix = s_sel[0];
-          rem = s_sel[1];
-          mask |= 255u << shift;
-        }
-        thr = prefix;
-        if (threadIdx.x == 0 && thr < spec) atomicOr(err, kErrSpec);
-      } else if (threadIdx.x == 0 && spec && !s_over) {
-        atomicOr(err, kErrSpec);  // fewer than k kept: the bound may have dropped some
-      }
-      // Compact key >= T into the tail slots.
-      __shared__ uint32_t s_m;
-      if (threadIdx.x == 0) s_m = 0;
-      __syncthreads();
-      float* cs = s + (MERGE_N - kSelMax);
-      int64_t* cid = id + (MERGE_N - kSelMax);
-      for (uint32_t e = threadIdx.x; e < n; e += MERGE_THREADS) {
-        if (score_key(s[e]) >= thr) {
-          const uint32_t slot = atomicAdd(&s_m, 1u);
-          if (slot < kSelMax) { cs[slot] = s[e]; cid[slot] = id[e]; }
-        }
-      }
-      __syncthreads();
-      const uint32_t m = s_m;
-      if (m <= kSelMax) {
-        // Exact rank of each selected entry (score desc, id asc); the best k
-        // go straight to their output slots.
-        const float qn = s_qn;
-        if (threadIdx.x < m) {
-          const float x = cs[threadIdx.x];
-          const int64_t g = cid[threadIdx.x];
-          uint32_t rank = 0;
-          for (uint32_t j = 0; j < m; ++j) rank += better64(cs[j], cid[j], x, g) ? 1u : 0u;
-          if (rank < k) {
-            out_d[size_t(q) * k + rank] = l2 ? qn - x : x;
-            out_id[size_t(q) * k + rank] = g;
-          }
-        }
-        for (uint32_t i = m + threadIdx.x; i < k; i += MERGE_THREADS) {
-          out_d[size_t(q) * k + i] = l2 ? INFINITY : -INFINITY;
-          out_id[size_t(q) * k + i] = -1;
-        }
-        return;
-      }
-    }
+    if (n <= MERGE_N - kSelMax && select_out(n)) return;
     if (n <= MERGE_N) {
       // Too many ties at the k-th score for the rank pass: sort the
       // survivors (already in [0, n)).
@@ -920,6 +930,26 @@ __global__ void __launch_bounds__(MERGE_THREADS) k_merge(const float* part_s, co
       bitonic_sort(s, id, min(n_sort, MERGE_N));
     }
   } else {
+    if (total <= MERGE_N - kSelMax) {
+      // Valid entries only (padding would tie with padding in the rank pass).
+      if (threadIdx.x == 0) s_m = 0;
+      __syncthreads();
+      for (uint32_t c = threadIdx.x; c < total; c += MERGE_THREADS) {
+        const uint32_t pidx = c / k, e = c % k;
+        const size_t g = (size_t(pidx) * n_queries + q) * k + e;
+        const int64_t i = part_id[g];
+        if (i >= 0) {
+          const float x = part_s[g];
+          const uint32_t slot = atomicAdd(&s_m, 1u);
+          s[slot] = kind == 0 ? x : (l2 ? -x : x);
+          id[slot] = i;
+        }
+      }
+      __syncthreads();
+      const uint32_t n_ok = s_m;
+      __syncthreads();  // every thread has n_ok before select_out resets s_m
+      if (select_out(n_ok)) return;
+    }
     uint64_t pos = 0;
     for (uint32_t i = threadIdx.x; i < MERGE_N; i += MERGE_THREADS) load(pos + i, i);
     pos += MERGE_N;
