@@ -70,11 +70,25 @@ static_assert(SMEM_TOTAL <= 232448, "shared memory per block");
 constexpr uint32_t TMEM_COLS = 512;                     // two 256-column accumulators
 constexpr uint32_t kIdesc = idesc_f16_f32(BM, BN);
 
+// The search's shape, decided on the device from the pass count so that the
+// host never waits for it: which rows are searched and how they are tiled.
+struct SearchPlan {
+  uint32_t n_rows;      // rows searched (shard rows when dense, passing rows when compacted)
+  uint32_t n_tiles;     // BN-row tiles
+  uint32_t tps;         // tiles per slice
+  uint32_t dense;       // 1: the shard's rows with the pass bitset; 0: the compacted rows
+  uint32_t spec_j;      // rank of the speculative bound in the prologue sample (0: none)
+  uint32_t spec_tiles;  // prologue tiles per slice
+};
+
 struct TopkParams {
-  uint32_t n_rows, n_queries, k, metric;
-  uint32_t n_tiles, tiles_per_slice;
-  const uint32_t* pass;  // local pass bitset, null = every row passes
-  const float* norms;    // squared row norms (L2)
+  uint32_t n_queries, k, metric;
+  const SearchPlan* plan;
+  const uint32_t* pass;  // shard pass bitset (dense plans; null = every row passes)
+  const float* norms;    // squared shard row norms (L2, dense plans)
+  const float* comp_norms;  // squared norms of the compacted rows (L2, compacted plans)
+  const uint32_t* guard; // non-null: run only if this error word has kErrOverflow/kErrSpec set
+  uint32_t spec_capable; // the prologue launch and k_spec run before this search
   float* list_s;         // per-query sorted lists: [cta][BM][2][k]
   uint32_t* list_r;
   float* part_s;         // [slice][Q][k] internal scores
@@ -88,27 +102,26 @@ struct TopkParams {
   uint32_t* pub;         // [Q][n_lists] published j-th best of every partial list (score keys)
   uint32_t n_lists;      // partial lists per query (2 per slice)
   uint32_t jth;          // ceil(k / n_lists)
-  const uint32_t* row_map;  // compacted row -> shard row (null: identity)
+  const uint32_t* row_map;  // compacted row -> shard row (compacted plans)
   uint32_t append;       // 1: survivors go to per-query candidate arrays, no list merges
   uint32_t cap;          // candidate slots per (query, list) (append mode)
   uint32_t keeper_ns;    // bound keeper refresh period
   float* cand_s;         // [Q][n_lists][cap]
   uint32_t* cand_r;
   uint32_t* cand_cnt;    // [Q][n_lists] entries appended (may exceed cap: overflow)
-  // Speculative bound (append mode). A prologue launch (prologue_only) runs
-  // the publish-only tiles and every list writes its best three scores to
-  // pub_top [list * 3 + i][Q]; k_spec turns their union into spec_used [Q];
-  // the main launch (no_prologue) starts with that bound. The merge verifies it.
+  // Speculative bound (append mode, plan spec_j > 0). A prologue launch
+  // (prologue_only) runs the publish-only tiles and every list writes its
+  // best three scores to pub_top [list * 3 + i][Q]; k_spec turns their union
+  // into spec_used [Q]; the main launch starts with that bound and skips its
+  // own publish-only tiles. The merge verifies it.
   uint32_t prologue_only;
-  uint32_t prologue_tiles;  // tiles per slice of the prologue launch
-  uint32_t no_prologue;
   uint32_t* pub_top;
   const uint32_t* spec_used;
 };
 
 constexpr uint32_t kErrOverflow = 64u;  // a candidate array filled up (append mode)
-constexpr uint32_t kErrSpec = 128u;
-constexpr uint32_t kPrologueTiles = 4;  // publish-only tiles at the start of each slice (append mode)     // a query's speculative bound was above its k-th best
+constexpr uint32_t kErrSpec = 128u;      // a query's speculative bound was above its k-th best
+constexpr uint32_t kPrologueTiles = 4;  // publish-only tiles at the start of each slice (append mode)
 
 // Order-preserving map float -> uint32 (larger float -> larger key); 0 is
 // below every real score and decodes to -inf.
@@ -228,8 +241,19 @@ __device__ __forceinline__ float pick32(const float* v, uint32_t j)
 template <bool APPEND>
 __global__ void __launch_bounds__(THREADS, 1)
     k_topk(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tdb,
-           TopkParams p)
+           const __grid_constant__ CUtensorMap tdb_comp, TopkParams p)
 {
+  // A fallback search runs only when the first pass asked for it.
+  if (p.guard && !(*reinterpret_cast<const volatile uint32_t*>(p.guard) & (kErrOverflow | kErrSpec))) return;
+  const SearchPlan pl = *p.plan;
+  const bool use_spec = APPEND && p.spec_capable && pl.spec_j != 0;
+  if (p.prologue_only && !use_spec) return;  // no speculative bound for this plan
+  const uint32_t n_rows = pl.n_rows;
+  const uint32_t* pass = pl.dense ? p.pass : nullptr;
+  const float* norms = pl.dense ? p.norms : p.comp_norms;
+  const uint32_t* row_map = pl.dense ? nullptr : p.row_map;
+  const CUtensorMap* tdbp = pl.dense ? &tdb : &tdb_comp;
+  const uint32_t* spec_used = use_spec ? p.spec_used : nullptr;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -251,13 +275,14 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t qt = blockIdx.x, slice = blockIdx.y;
-  const uint32_t t0 = slice * p.tiles_per_slice;
-  const uint32_t t1 = min(p.n_tiles, t0 + p.tiles_per_slice);
+  const uint32_t t0 = slice * pl.tps;
+  const uint32_t t1 = max(t0, min(pl.n_tiles, t0 + pl.tps));  // slices past the rows get no tiles
   // Tile schedule. In append mode the first D tiles of the slice run first
   // in publish-only mode (their best scores feed the shared bound, nothing is
   // kept), then every tile runs with the bound, those D last.
   const uint32_t T = t1 - t0;
-  const uint32_t D = (APPEND && !p.no_prologue) ? min(T, p.prologue_only ? p.prologue_tiles : kPrologueTiles) : 0u;
+  const uint32_t D = (APPEND && (p.prologue_only || !use_spec))
+                         ? min(T, p.prologue_only ? pl.spec_tiles : kPrologueTiles) : 0u;
   const uint32_t n_it = p.prologue_only ? D : T + D;
   auto tile_of = [&](uint32_t it) { return it < T ? t0 + it : t0 + (it - T); };
 
@@ -272,7 +297,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   // the first tiles are filtered before the keeper's first refresh.
   for (uint32_t i = threadIdx.x; i < BM; i += THREADS) {
     const uint32_t q2 = qt * BM + i;
-    s_bound[i] = (p.spec_used && q2 < p.n_queries) ? key_score(__ldcg(p.spec_used + q2)) : -INFINITY;
+    s_bound[i] = (spec_used && !p.prologue_only && q2 < p.n_queries) ? key_score(__ldcg(spec_used + q2)) : -INFINITY;
   }
   if (warp == 0) tmem_alloc(tmem_slot, TMEM_COLS);
   tc_fence_before();
@@ -284,7 +309,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ---------------- TMA producer
     if (lane == 0) {
       prefetch_tmap(&tq);
-      prefetch_tmap(&tdb);
+      prefetch_tmap(tdbp);
       mbar_expect_tx(q_full, 2 * KB_BYTES_Q);
       tma_load_2d(&tq, q_full, sQ, 0, int32_t(qt * BM));
       tma_load_2d(&tq, q_full, sQ + KB_BYTES_Q, 64, int32_t(qt * BM));
@@ -293,8 +318,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (!mbar_wait(empty + s, ((it / STAGES) & 1u) ^ 1u, p.err, 1u)) break;
         uint8_t* dst = sDB + s * STAGE_BYTES;
         mbar_expect_tx(full + s, STAGE_BYTES);
-        tma_load_2d(&tdb, full + s, dst, 0, int32_t(t * BN));
-        tma_load_2d(&tdb, full + s, dst + KB_BYTES_DB, 64, int32_t(t * BN));
+        tma_load_2d(tdbp, full + s, dst, 0, int32_t(t * BN));
+        tma_load_2d(tdbp, full + s, dst + KB_BYTES_DB, 64, int32_t(t * BN));
       }
     }
   } else if (warp == 1) {
@@ -328,7 +353,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
     for (uint32_t i = 0; i < BM / 32; ++i) {
       const uint32_t q2 = qt * BM + lane + 32 * i;
-      spec[i] = (p.spec_used && q2 < p.n_queries) ? key_score(__ldcg(p.spec_used + q2)) : -INFINITY;
+      spec[i] = (spec_used && !p.prologue_only && q2 < p.n_queries) ? key_score(__ldcg(spec_used + q2)) : -INFINITY;
     }
     for (uint32_t iter = 0; iter < kSpinLimit; ++iter) {
 #pragma unroll
@@ -422,7 +447,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     // A main launch after a prologue launch keeps the prologue's published
     // values (valid lower bounds) until this list beats them.
     uint32_t published =
-        (APPEND && p.no_prologue && valid_q) ? __ldcg(p.pub + size_t(slice * EPI_PARTS + chalf) * p.n_queries + qi) : 0u;
+        (use_spec && !p.prologue_only && valid_q) ? __ldcg(p.pub + size_t(slice * EPI_PARTS + chalf) * p.n_queries + qi) : 0u;
     const bool fast_pub = p.jth <= 3;
     const uint32_t my_list = slice * EPI_PARTS + chalf;
     uint32_t nc = 0;  // candidates this (query, list) appended (append mode)
@@ -495,7 +520,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           else { top3 = x; }
         }
       };
-      const bool whole = APPEND && !l2 && !p.pass && row0 + BN <= p.n_rows && p.debug == 0;
+      const bool whole = APPEND && !l2 && !pass && row0 + BN <= n_rows && p.debug == 0;
       if (whole) {
         // Every row of this part passes: one 64-column TMEM load and one
         // 6-level max tree for the part's two chunks.
@@ -523,9 +548,9 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll 1
         for (uint32_t c = chalf * PART_CHUNKS; c < (p.debug == 1 ? 0u : (chalf + 1) * PART_CHUNKS); ++c) {
           const uint32_t r0 = row0 + c * 32;
-          if (r0 >= p.n_rows) break;
-          uint32_t m = p.pass ? __ldg(p.pass + (r0 >> 5)) : 0xFFFFFFFFu;
-          const uint32_t left = p.n_rows - r0;
+          if (r0 >= n_rows) break;
+          uint32_t m = pass ? __ldg(pass + (r0 >> 5)) : 0xFFFFFFFFu;
+          const uint32_t left = n_rows - r0;
           if (left < 32) m &= (1u << left) - 1u;
           if (m == 0) continue;
           float v[32];
@@ -533,7 +558,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (l2) {
 #pragma unroll
             for (int j = 0; j < 32; ++j)  // rows past the mask (and n_rows) are never read
-              v[j] = ((m >> j) & 1u) ? 2.f * v[j] - __ldg(p.norms + r0 + j) : -INFINITY;
+              v[j] = ((m >> j) & 1u) ? 2.f * v[j] - __ldg(norms + r0 + j) : -INFINITY;
           }
           // Fast path: the best passing score of the chunk against the bound
           // (a 5-level max tree, not a 32-long dependency chain).
@@ -597,7 +622,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         p.part_s[base + i] = i < f_cnt ? ls[i] : -INFINITY;
         const uint32_t r = i < f_cnt ? lr[i] : 0u;
         p.part_id[base + i] =
-            i < f_cnt ? int64_t(p.row_map ? __ldg(p.row_map + r) : r) + int64_t(p.row_offset) : int64_t(-1);
+            i < f_cnt ? int64_t(row_map ? __ldg(row_map + r) : r) + int64_t(p.row_offset) : int64_t(-1);
       }
     }
   }
@@ -606,13 +631,57 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 0) tmem_dealloc(tmem, TMEM_COLS);
 }
 
+// One thread: the search plan from the pass count (`count`, null = every
+// shard row passes). Below half density the passing rows are compacted and
+// searched; otherwise the shard is searched with the pass bitset. Then the
+// tiling over `slices`, and the speculative bound's rank: the prologue sees
+// about `sample` of the searched rows, and the spec_j-th best of the union
+// of every list's best three has fewer than k rows at or above it with
+// probability P(Poisson(k * sample / rows) >= spec_j), taken below 1e-9
+// (each list's best three only lower the value). spec_override (measurement
+// and tests) forces the rank when >= 0; tiles_override the prologue length.
+__global__ void k_plan(const uint32_t* count, uint32_t shard_rows, uint32_t slices, uint32_t n_lists,
+                       uint32_t k, uint32_t spec_capable, int spec_override, int tiles_override,
+                       SearchPlan* plan)
+{
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  SearchPlan pl{};
+  const uint32_t n_pass = count ? *count : shard_rows;
+  pl.dense = (count == nullptr || uint64_t(n_pass) * 2 > shard_rows) ? 1u : 0u;
+  pl.n_rows = pl.dense ? shard_rows : n_pass;
+  pl.n_tiles = (pl.n_rows + BN - 1) / BN;
+  pl.tps = max(1u, (pl.n_tiles + slices - 1) / slices);
+  pl.spec_tiles = max(kPrologueTiles, min(24u, pl.tps / 8));  // at most an eighth of a slice
+  if (tiles_override > 0) pl.spec_tiles = uint32_t(tiles_override);
+  if (spec_capable && pl.n_rows > 0 && 3 * n_lists <= 256) {
+    const double sample = double(min(uint64_t(pl.n_rows), uint64_t(slices) * min(pl.tps, pl.spec_tiles) * BN));
+    const double f = sample / double(pl.n_rows);
+    if (f <= 0.5) {
+      const double lam = double(k) * f;
+      // Smallest j >= 1 with P(X >= j) = 1 - P(X < j) below 1e-9, X ~ Poisson(lam).
+      double term = exp(-lam), below = 0.0;  // P(X = j), P(X < j)
+      uint32_t j = 0;
+      for (; j <= 3 * n_lists; ++j) {
+        if (j >= 1 && 1.0 - below < 1e-9) break;
+        below += term;
+        term *= lam / double(j + 1);
+      }
+      if (j <= 3 * n_lists) pl.spec_j = j;
+    }
+    if (spec_override >= 0) pl.spec_j = min(uint32_t(spec_override), 3 * n_lists);
+  }
+  *plan = pl;
+}
+
 // One warp per query: spec_used[q] = the j-th largest of the n_vals (<= 256)
 // published keys pub_top[i][q] (0 when fewer than j are non-zero).
 __global__ void __launch_bounds__(128) k_spec(const uint32_t* pub_top, uint32_t n_vals, uint32_t n_queries,
-                                              uint32_t j, uint32_t* spec_used)
+                                              const SearchPlan* plan, uint32_t* spec_used)
 {
   const uint32_t q = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (q >= n_queries) return;
+  const uint32_t j = plan->spec_j;
+  if (j == 0) return;  // no speculative bound: the searches ignore spec_used
   uint32_t v[8];
 #pragma unroll
   for (uint32_t e = 0; e < 8; ++e) {
@@ -674,8 +743,15 @@ __global__ void __launch_bounds__(MERGE_THREADS) k_merge(const float* part_s, co
                                                          const uint32_t* row_map, uint64_t row_offset,
                                                          const uint32_t* pub, uint32_t n_lists,
                                                          uint32_t n_rows, const uint32_t* spec_used,
-                                                         uint32_t* err)
+                                                         uint32_t* err, const SearchPlan* plan,
+                                                         const uint32_t* guard)
 {
+  if (guard && !(*reinterpret_cast<const volatile uint32_t*>(guard) & (kErrOverflow | kErrSpec))) return;
+  if (plan) {  // a search's candidates: rows and row ids as the plan decided
+    n_rows = plan->n_rows;
+    if (plan->dense) row_map = nullptr;
+    if (plan->spec_j == 0) spec_used = nullptr;
+  }
   extern __shared__ uint8_t smem_raw[];
   float* s = reinterpret_cast<float*>(smem_raw);
   int64_t* id = reinterpret_cast<int64_t*>(smem_raw + MERGE_N * 4);
@@ -1082,6 +1158,8 @@ __global__ void __launch_bounds__(kWordTile) k_pass_tile_sums(const uint32_t* pa
 }
 
 // idx[] = shard rows whose filter bit is set, ascending; *total = count.
+// Nothing is written when the count exceeds cap_rows (the plan then searches
+// the shard densely).
 // With `comp`, the block then copies its rows: comp[i] = db[idx[i]]
 // (16 threads x 16 B per 128-dim row), so the gather needs no launch of its
 // own and starts as soon as the block's indices are known.
@@ -1089,7 +1167,7 @@ __global__ void __launch_bounds__(kWordTile) k_pass_compact(const uint32_t* pass
                                                             const uint32_t* tile_sums, uint32_t n_tiles,
                                                             uint32_t* idx, uint32_t* total,
                                                             const float* norms, float* comp_norms,
-                                                            const uint4* db, uint4* comp)
+                                                            const uint4* db, uint4* comp, uint32_t cap_rows)
 {
   __shared__ uint32_t s_red[32];
   // Rows of the earlier word tiles: the block's first output slot.
@@ -1102,6 +1180,7 @@ __global__ void __launch_bounds__(kWordTile) k_pass_compact(const uint32_t* pass
   const uint32_t base = block_sum<kWordTile>(before, s_red);
   const uint32_t everything = block_sum<kWordTile>(all, s_red);
   if (blockIdx.x == 0 && threadIdx.x == 0) *total = everything;
+  if (everything > cap_rows) return;  // dense plan: the shard is searched with the bitset
   const uint64_t w = uint64_t(blockIdx.x) * kWordTile + threadIdx.x;
   uint32_t x = w < n_words ? pass[w] : 0u;
   uint32_t tot;
@@ -1130,12 +1209,6 @@ __global__ void __launch_bounds__(kWordTile) k_pass_compact(const uint32_t* pass
     for (uint32_t u = 0; u < U; ++u)
       if (dst[u] != 0xFFFFFFFFu) comp[size_t(dst[u])] = v[u];
   }
-}
-
-__global__ void k_fill_empty(float* d, int64_t* ids, uint64_t n, float v)
-{
-  const uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i < n) { d[i] = v; ids[i] = -1; }
 }
 
 // ------------------------------------------------------------------- host
@@ -1182,7 +1255,8 @@ void merge_launch(const float* ps, const int64_t* pid, uint32_t parts, uint32_t 
                   cudaStream_t s, const uint32_t* cand_cnt = nullptr, uint32_t cap = 0,
                   const uint32_t* cand_r = nullptr, const uint32_t* row_map = nullptr,
                   uint64_t row_offset = 0, const uint32_t* pub = nullptr, uint32_t n_lists = 0,
-                  uint32_t n_rows = 0, const uint32_t* spec_used = nullptr, uint32_t* err = nullptr)
+                  uint32_t n_rows = 0, const uint32_t* spec_used = nullptr, uint32_t* err = nullptr,
+                  const SearchPlan* plan = nullptr, const uint32_t* guard = nullptr)
 {
   static std::once_flag once;
   const size_t smem = MERGE_N * 12;
@@ -1192,7 +1266,7 @@ void merge_launch(const float* ps, const int64_t* pid, uint32_t parts, uint32_t 
   ProfileScope prof(CR_KERNEL_TOPK_MERGE, s);
   k_merge<<<nq, MERGE_THREADS, smem, s>>>(ps, pid, parts, nq, k, metric, kind, queries, dim, od, oi,
                                           cand_cnt, cap, cand_r, row_map, row_offset, pub, n_lists, n_rows,
-                                          spec_used, err);
+                                          spec_used, err, plan, guard);
   CR_CUDA(cudaGetLastError());
 }
 
@@ -1253,33 +1327,93 @@ struct Trace {
   Trace() { for (auto& e : ev) e = nullptr; }
 };
 
-// A small page-locked host buffer per thread for the counts the host reads
-// back (a pageable destination makes the copy slower).
-static uint32_t* pinned_words()
-{
-  thread_local uint32_t* buf = nullptr;
-  if (!buf) CR_CUDA(cudaMallocHost(reinterpret_cast<void**>(&buf), 64));
-  return buf;
-}
-
 // The tcgen05 search over `n_rows` rows (optionally masked by `pass`, row
 // ids optionally translated by `row_map`) plus the per-query merge.
-static void run_topk_core(const uint16_t* d_db, const float* norms, uint64_t n_rows, const uint32_t* pass,
-                          const uint32_t* row_map, const uint16_t* d_queries, uint32_t n_queries,
-                          uint64_t row_offset, uint32_t k, int metric, float* d_out_dist,
-                          int64_t* d_out_ids, cudaStream_t s, bool allow_append = true,
-                          bool allow_spec = true)
+// Device-side failures of a search (bounded waits that ran out) are copied to
+// a small ring of page-locked words per host thread and reported by the next
+// call on that thread, or by cr_filtered_topk_check, without making the
+// search itself wait for the device.
+struct ErrorRing {
+  static constexpr int kSlots = 8;
+  uint32_t* words = nullptr;  // [kSlots][2]
+  cudaEvent_t ev[kSlots] = {};
+  bool pending[kSlots] = {};
+  int next = 0;
+  static ErrorRing& get()
+  {
+    thread_local ErrorRing r;
+    return r;
+  }
+  // Reports completed slots; with `wait`, waits for every slot first.
+  void check(bool wait)
+  {
+    for (int i = 0; i < kSlots; ++i) {
+      if (!pending[i]) continue;
+      if (wait) CR_CUDA(cudaEventSynchronize(ev[i]));
+      else if (cudaEventQuery(ev[i]) != cudaSuccess) continue;
+      pending[i] = false;
+      // First pass: everything but the fallback requests; fallback: everything.
+      const uint32_t bad = (words[2 * i] & ~(kErrOverflow | kErrSpec)) | words[2 * i + 1];
+      if (bad)
+        fail(CR_ERR_DEVICE, "cr_filtered_topk: a pipeline wait timed out on the device (code " +
+                                std::to_string(bad) + ")");
+    }
+  }
+  void record(const uint32_t* d_err0, const uint32_t* d_err1, cudaStream_t s)
+  {
+    if (!words) {
+      CR_CUDA(cudaMallocHost(reinterpret_cast<void**>(&words), kSlots * 2 * 4));
+      for (auto& e : ev) CR_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    }
+    const int i = next;
+    next = (next + 1) % kSlots;
+    if (pending[i]) {  // more than kSlots searches in flight: wait for the oldest
+      CR_CUDA(cudaEventSynchronize(ev[i]));
+      const uint32_t bad = (words[2 * i] & ~(kErrOverflow | kErrSpec)) | words[2 * i + 1];
+      pending[i] = false;
+      if (bad) fail(CR_ERR_DEVICE, "cr_filtered_topk: a pipeline wait timed out on the device (code " +
+                                       std::to_string(bad) + ")");
+    }
+    CR_CUDA(cudaMemcpyAsync(words + 2 * i, d_err0, 4, cudaMemcpyDeviceToHost, s));
+    if (d_err1) CR_CUDA(cudaMemcpyAsync(words + 2 * i + 1, d_err1, 4, cudaMemcpyDeviceToHost, s));
+    else words[2 * i + 1] = 0;
+    CR_CUDA(cudaEventRecord(ev[i], s));
+    pending[i] = true;
+  }
+};
+
+// What a search reads: the shard (dense plans) and the compacted passing rows
+// (compacted plans); the plan on the device says which.
+struct SearchInput {
+  const uint16_t* db;
+  uint64_t shard_rows;
+  const float* norms;      // shard norms (L2)
+  const uint32_t* pass;    // shard pass bitset, null = every row passes
+  const uint16_t* comp;    // compacted rows (null: no compaction)
+  uint64_t comp_cap;       // rows comp can hold
+  const float* comp_norms;
+  const uint32_t* idx;     // compacted row -> shard row
+  const SearchPlan* plan;
+};
+
+// One search over the planned rows plus the per-query merge, stream-ordered.
+// Append mode (candidate arrays, speculative bound) unless disabled; `guard`
+// makes every kernel of it a no-op unless that error word asks for a redo;
+// device-side failures land in `err` (16 bytes, zeroed here).
+static void run_search(const SearchInput& in, const uint16_t* d_queries, uint32_t n_queries, uint64_t row_offset,
+                       uint32_t k, int metric, float* d_out_dist, int64_t* d_out_ids, cudaStream_t s,
+                       bool allow_append, bool allow_spec, const uint32_t* guard, uint32_t* err,
+                       bool* used_append)
 {
   static std::once_flag once;
   std::call_once(once, [] {
     cudaFuncSetAttribute(k_topk<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(SMEM_TOTAL));
     cudaFuncSetAttribute(k_topk<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(SMEM_TOTAL));
   });
-  const uint32_t n_tiles = div_up(n_rows, BN);
+  // Grid: query tiles x slices, sized for the largest plan (every shard row).
+  const uint32_t max_tiles = std::max<uint32_t>(1u, div_up(in.shard_rows, BN));
   const uint32_t qtiles = div_up(n_queries, BM);
-  const uint32_t want_slices = std::max(1, sm_count() / int(qtiles));
-  const uint32_t tps = div_up(n_tiles, std::min<uint32_t>(want_slices, n_tiles));
-  const uint32_t slices = div_up(n_tiles, tps);
+  const uint32_t slices = std::min<uint32_t>(std::max(1, sm_count() / int(qtiles)), max_tiles);
   const size_t ctas = size_t(qtiles) * slices;
   const size_t list_b = ctas * EPI_PARTS * 2 * k * BM * 4;
   const size_t part_b = size_t(slices) * EPI_PARTS * n_queries * k;
@@ -1290,65 +1424,39 @@ static void run_topk_core(const uint16_t* d_db, const float* norms, uint64_t n_r
   // Append mode needs the register-tracked list bounds (jth <= 3); its
   // candidate arrays hold up to `cap` survivors per query.
   const bool append = allow_append && jth <= 3 && n_lists <= kMaxListsMerge;
+  *used_append = append;
   const uint32_t cap = append ? std::max<uint32_t>(256u, div_up(std::max<uint32_t>(32768u, 128u * k), n_lists)) : 0u;
   const size_t cand_b = append ? size_t(n_queries) * n_lists * cap * 4 : 0;
-  // Speculative bound: the prologue sees about `sample` of the rows; the
-  // spec_j-th best of the union of every list's top 3 then has fewer than k
-  // rows at or above it with probability P(Poisson(k * sample / n_rows) >=
-  // spec_j) (taken below 1e-9), each list's top 3 only lowering the value.
-  uint32_t spec_j = 0;
-  // Prologue launch length: up to 24 tiles per slice, at most an eighth of
-  // the slice (at least 4).
-  uint32_t spec_tiles = std::max(kPrologueTiles, std::min(24u, tps / 8));
-  if (const char* st = getenv("CR_TOPK_SPEC_TILES")) spec_tiles = std::max(1, atoi(st));  // measurement
-  if (append && allow_spec && 3 * n_lists <= 256) {
-    const uint64_t sample = std::min<uint64_t>(n_rows, uint64_t(slices) * std::min(tps, spec_tiles) * BN);
-    const double f = double(sample) / double(n_rows);
-    if (f <= 0.5) {
-      const double lam = double(k) * f;
-      // P(X >= j) for X ~ Poisson(lam), summed from j upward.
-      auto tail = [&](uint32_t j) {
-        double term = std::exp(-lam), acc = 0.0;
-        for (uint32_t i = 1; i <= j; ++i) term *= lam / double(i);
-        for (uint32_t i = j; i < j + 400; ++i) { acc += term; term *= lam / double(i + 1); }
-        return acc;
-      };
-      uint32_t j = std::max<uint32_t>(1u, uint32_t(lam));
-      while (j <= 3 * n_lists && tail(j) >= 1e-9) ++j;
-      if (j <= 3 * n_lists) spec_j = j;
-    }
-    // Test hook: force the rank (1 = the sample's best, which is almost
-    // surely above the k-th best and so exercises the verification) or
-    // switch the bound off (0).
-    if (const char* sj = getenv("CR_TOPK_SPEC_J")) spec_j = std::min<uint32_t>(uint32_t(atoi(sj)), 3 * n_lists);
-  }
-  const size_t spec_b = spec_j ? size_t(n_queries) * n_lists * 3 * 4 + size_t(n_queries) * 4 + 16 : 0;
-  Scratch scr(list_b * 2 + cbuf_b * 2 + part_b * 12 + pub_b + cand_b * 2 + size_t(n_queries) * n_lists * 4 +
-                  size_t(n_queries) * 8 + 64 + 512 + spec_b + 256, s);
+  const bool spec_capable = append && allow_spec && 3 * n_lists <= 256;
+  const size_t spec_b = spec_capable ? size_t(n_queries) * 4 + 16 : 0;
+  const size_t top_b = spec_capable ? size_t(n_queries) * n_lists * 3 * 4 : 0;
+  const size_t cnt_b = append ? size_t(n_queries) * n_lists * 4 : 0;
+  // Everything that must start at zero sits in one block at the front, cleared
+  // by one memset: per-query shared thresholds, published bounds, candidate
+  // counts, published best three.
+  const size_t zero_b = size_t(n_queries) * 4 + pub_b + cnt_b + top_b;
+  Scratch scr(zero_b + 256 + list_b * 2 + cbuf_b * 2 + part_b * 12 + cand_b * 2 + spec_b + 256, s);
   char* p = scr.as<char>();
   TopkParams tp{};
-  // Everything that must start at zero sits in one block at the front, cleared
-  // by one memset: error word + counters, per-query shared thresholds,
-  // published bounds, candidate counts, published best three.
-  const size_t zero_b = 16 + size_t(n_queries) * 4 + pub_b + (append ? size_t(n_queries) * n_lists * 4 : 0) +
-                        (spec_j ? size_t(n_queries) * n_lists * 3 * 4 : 0);
-  tp.err = reinterpret_cast<uint32_t*>(p); p += 16;
+  tp.err = err;
   tp.shared_thr = reinterpret_cast<uint32_t*>(p); p += size_t(n_queries) * 4;
   tp.pub = reinterpret_cast<uint32_t*>(p); p += pub_b;
-  if (append) { tp.cand_cnt = reinterpret_cast<uint32_t*>(p); p += size_t(n_queries) * n_lists * 4; }
-  if (spec_j) { tp.pub_top = reinterpret_cast<uint32_t*>(p); p += size_t(n_queries) * n_lists * 3 * 4; }
-  CR_CUDA(cudaMemsetAsync(tp.err, 0, zero_b, s));
+  if (append) { tp.cand_cnt = reinterpret_cast<uint32_t*>(p); p += cnt_b; }
+  if (spec_capable) { tp.pub_top = reinterpret_cast<uint32_t*>(p); p += top_b; }
+  CR_CUDA(cudaMemsetAsync(err, 0, 16, s));
+  CR_CUDA(cudaMemsetAsync(tp.shared_thr, 0, zero_b, s));
   p = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(p) + 255) & ~uintptr_t(255));
-  tp.n_rows = static_cast<uint32_t>(n_rows);
   tp.n_queries = n_queries;
   tp.k = k;
   tp.metric = metric;
-  tp.n_tiles = n_tiles;
-  tp.tiles_per_slice = tps;
+  tp.plan = in.plan;
   tp.row_offset = row_offset;
-  tp.pass = pass;
-  tp.norms = norms;
-  tp.row_map = row_map;
+  tp.pass = in.pass;
+  tp.norms = in.norms;
+  tp.comp_norms = in.comp_norms;
+  tp.row_map = in.idx;
+  tp.guard = guard;
+  tp.spec_capable = spec_capable ? 1u : 0u;
   tp.list_s = reinterpret_cast<float*>(p); p += list_b;
   tp.list_r = reinterpret_cast<uint32_t*>(p); p += list_b;
   tp.buf_s = reinterpret_cast<float*>(p); p += cbuf_b;
@@ -1362,9 +1470,8 @@ static void run_topk_core(const uint16_t* d_db, const float* norms, uint64_t n_r
     tp.cand_r = reinterpret_cast<uint32_t*>(p); p += cand_b;
   }
   uint32_t* spec_used = nullptr;
-  if (spec_j) {
-    spec_used = reinterpret_cast<uint32_t*>(p); p += size_t(n_queries) * 4 + 16;
-  }
+  if (spec_capable) { spec_used = reinterpret_cast<uint32_t*>(p); p += spec_b; }
+  tp.spec_used = spec_used;
   tp.part_id = reinterpret_cast<int64_t*>(p); p += part_b * 8;
   tp.part_s = reinterpret_cast<float*>(p); p += part_b * 4;
   if (const char* dbg = getenv("CR_TOPK_DEBUG")) tp.debug = uint32_t(atoi(dbg));
@@ -1372,69 +1479,41 @@ static void run_topk_core(const uint16_t* d_db, const float* norms, uint64_t n_r
   if (const char* kn = getenv("CR_TOPK_KEEPER_NS")) tp.keeper_ns = uint32_t(atoi(kn));
   Trace::get().mark("setup", s);
   const CUtensorMap tq = make_map(d_queries, n_queries, BM);
-  const CUtensorMap tdb = make_map(d_db, n_rows, BN);
+  const CUtensorMap tdb = make_map(in.db, in.shard_rows, BN);
+  const CUtensorMap tcomp = in.comp ? make_map(in.comp, std::max<uint64_t>(1, in.comp_cap), BN) : tdb;
+  const dim3 grid(qtiles, slices);
   {
-    ProfileScope prof(CR_KERNEL_TOPK, s);
-    if (spec_j) {
+    ProfileScope prof(guard ? -1 : CR_KERNEL_TOPK, s);
+    if (spec_capable) {
       // Prologue launch (publish-only tiles), the speculative bound per
-      // query, then the main launch starting from it.
+      // query, then the main launch starting from it (all no-ops when the
+      // plan has no speculative bound).
       TopkParams pro = tp;
       pro.prologue_only = 1;
-      pro.prologue_tiles = spec_tiles;
-      k_topk<true><<<dim3(qtiles, slices), THREADS, SMEM_TOTAL, s>>>(tq, tdb, pro);
-      k_spec<<<div_up(n_queries, 4u), 128, 0, s>>>(tp.pub_top, 3 * n_lists, n_queries, spec_j, spec_used);
-      tp.no_prologue = 1;
-      tp.spec_used = spec_used;
+      k_topk<true><<<grid, THREADS, SMEM_TOTAL, s>>>(tq, tdb, tcomp, pro);
+      k_spec<<<div_up(n_queries, 4u), 128, 0, s>>>(tp.pub_top, 3 * n_lists, n_queries, in.plan, spec_used);
     }
     Trace::get().mark("prologue_spec", s);
-    if (append) k_topk<true><<<dim3(qtiles, slices), THREADS, SMEM_TOTAL, s>>>(tq, tdb, tp);
-    else k_topk<false><<<dim3(qtiles, slices), THREADS, SMEM_TOTAL, s>>>(tq, tdb, tp);
+    if (append) k_topk<true><<<grid, THREADS, SMEM_TOTAL, s>>>(tq, tdb, tcomp, tp);
+    else k_topk<false><<<grid, THREADS, SMEM_TOTAL, s>>>(tq, tdb, tcomp, tp);
   }
   CR_CUDA(cudaGetLastError());
   if (append)
     merge_launch(tp.cand_s, nullptr, 0, n_queries, k, metric, 2, reinterpret_cast<const __half*>(d_queries),
-                 DIM, d_out_dist, d_out_ids, s, tp.cand_cnt, cap, tp.cand_r, row_map, row_offset, tp.pub,
-                 n_lists, tp.n_rows, spec_used, tp.err);
+                 DIM, d_out_dist, d_out_ids, s, tp.cand_cnt, cap, tp.cand_r, in.idx, row_offset, tp.pub,
+                 n_lists, 0, spec_used, err, in.plan, guard);
   else
-    merge_launch(tp.part_s, tp.part_id, slices * EPI_PARTS, n_queries, k, metric, 0,
-                 reinterpret_cast<const __half*>(d_queries), DIM, d_out_dist, d_out_ids, s);
-  Trace::get().mark("main_merge", s);
-  uint32_t* h_word = pinned_words();
-  CR_CUDA(cudaMemcpyAsync(h_word, tp.err, 4, cudaMemcpyDeviceToHost, s));
-  CR_CUDA(cudaStreamSynchronize(s));
-  uint32_t h_err = h_word[0];
-  if (tp.debug == 3) {
+    merge_launch(tp.part_s, tp.part_id, n_lists, n_queries, k, metric, 0,
+                 reinterpret_cast<const __half*>(d_queries), DIM, d_out_dist, d_out_ids, s, nullptr, 0, nullptr,
+                 nullptr, 0, nullptr, 0, 0, nullptr, nullptr, nullptr, guard);
+  Trace::get().mark(guard ? "fallback" : "main_merge", s);
+  if (tp.debug == 3) {  // measurement only: waits
     uint32_t c[4];
-    CR_CUDA(cudaMemcpy(c, tp.err, 16, cudaMemcpyDeviceToHost));
-    fprintf(stderr, "topk debug: lane flushes %u, warp slow paths / flush rounds %u, inserts %u, spec_j %u, err %u\n",
-            c[1], c[2], c[3], spec_j, c[0]);
-    if (spec_j) {
-      uint32_t sp[4];
-      float kd[4];
-      CR_CUDA(cudaMemcpy(sp, spec_used, 16, cudaMemcpyDeviceToHost));
-      for (int i = 0; i < 4; ++i)
-        CR_CUDA(cudaMemcpy(kd + i, d_out_dist + size_t(i) * k + k - 1, 4, cudaMemcpyDeviceToHost));
-      for (int i = 0; i < 4; ++i) {
-        const uint32_t key = sp[i];
-        const uint32_t bits = key == 0 ? 0xFF800000u : ((key & 0x80000000u) ? (key & 0x7FFFFFFFu) : ~key);
-        float f;
-        memcpy(&f, &bits, 4);
-        fprintf(stderr, "  q%d spec %.5f kth %.5f\n", i, f, kd[i]);
-      }
-    }
-    h_err = c[0];
+    CR_CUDA(cudaMemcpyAsync(c, err, 16, cudaMemcpyDeviceToHost, s));
+    CR_CUDA(cudaStreamSynchronize(s));
+    fprintf(stderr, "topk debug: lane flushes %u, warp slow paths / flush rounds %u, inserts %u, err %u\n", c[1],
+            c[2], c[3], c[0]);
   }
-  if (append && (h_err & (kErrOverflow | kErrSpec)) && !(h_err & ~(kErrOverflow | kErrSpec))) {
-    // A candidate array overflowed (degenerate score distribution, e.g.
-    // massive ties): redo exactly with per-list merging, which needs no
-    // candidate capacity. The speculative bound was too high for some query
-    // (a sample far from the rest of the rows): redo without it.
-    const bool overflow = (h_err & kErrOverflow) != 0;
-    run_topk_core(d_db, norms, n_rows, pass, row_map, d_queries, n_queries, row_offset, k, metric,
-                  d_out_dist, d_out_ids, s, !overflow, false);
-    return;
-  }
-  if (h_err) fail(CR_ERR_DEVICE, "cr_filtered_topk: pipeline wait timed out (code " + std::to_string(h_err) + ")");
 }
 
 extern "C" int cr_filtered_topk(const uint16_t* d_db, const float* d_db_norms, uint64_t n_rows,
@@ -1453,12 +1532,22 @@ extern "C" int cr_filtered_topk(const uint16_t* d_db, const float* d_db_norms, u
   CR_REQUIRE((reinterpret_cast<uintptr_t>(d_db) & 15u) == 0 &&
                  (reinterpret_cast<uintptr_t>(d_queries) & 15u) == 0,
              "cr_filtered_topk: db and queries must be 16-byte aligned");
+  ErrorRing::get().check(false);  // failures of earlier searches on this thread
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const bool l2 = metric == CR_METRIC_L2;
   Trace& tr = Trace::get();
   tr.on = getenv("CR_TOPK_TRACE") != nullptr;
   tr.n = 0;
   tr.mark("start", s);
+
+  // Control block for the whole call: plan, pass count, both searches' error
+  // words (the fallback reads the first one).
+  Scratch ctl(256, s);
+  SearchPlan* plan = reinterpret_cast<SearchPlan*>(ctl.as<char>());
+  uint32_t* count = reinterpret_cast<uint32_t*>(ctl.as<char>() + 64);
+  uint32_t* err0 = reinterpret_cast<uint32_t*>(ctl.as<char>() + 128);
+  uint32_t* err1 = reinterpret_cast<uint32_t*>(ctl.as<char>() + 192);
+  CR_CUDA(cudaMemsetAsync(count, 0, 4, s));
 
   // Squared norms of the shard rows (L2 only), computed here when not given.
   Scratch norm_scr((l2 && !d_db_norms) ? n_rows * 4 : 0, s);
@@ -1467,72 +1556,93 @@ extern "C" int cr_filtered_topk(const uint16_t* d_db, const float* d_db_norms, u
     row_norms(d_db, n_rows, norm_scr.as<float>(), s);
     norms = norm_scr.as<float>();
   }
-  if (!filter) {
-    run_topk_core(d_db, norms, n_rows, nullptr, nullptr, d_queries, n_queries, row_offset, k, metric,
-                  d_out_dist, d_out_ids, s);
-    return CR_OK;
-  }
-  // Shard-local pass bitset from the Roaring filter.
+  SearchInput in{};
+  in.db = d_db;
+  in.shard_rows = n_rows;
+  in.norms = norms;
+  in.plan = plan;
+  const uint32_t qtiles = div_up(n_queries, BM);
+  const uint32_t slices =
+      std::min<uint32_t>(std::max(1, sm_count() / int(qtiles)), std::max<uint32_t>(1u, div_up(n_rows, BN)));
+  const int spec_override = getenv("CR_TOPK_SPEC_J") ? atoi(getenv("CR_TOPK_SPEC_J")) : -1;  // tests
+  const int tiles_override = getenv("CR_TOPK_SPEC_TILES") ? atoi(getenv("CR_TOPK_SPEC_TILES")) : 0;  // measurement
+  const uint32_t jth = (k + slices * EPI_PARTS - 1) / (slices * EPI_PARTS);
+  const uint32_t spec_capable = (jth <= 3 && 3 * slices * EPI_PARTS <= 256) ? 1u : 0u;
+  // Pass bitset and compaction (filtered searches); their scratch lives to
+  // the end of the call.
   const uint64_t pass_words = (n_rows + 31) / 32;
   const uint32_t n_wtiles = div_up(pass_words, kWordTile);
-  Scratch pass_scr(pass_words * 4 + 16 + size_t(n_wtiles) * 4 + 16, s);
-  uint32_t* pass = pass_scr.as<uint32_t>();
-  uint32_t* d_total = pass + pass_words;
-  uint32_t* tiles = d_total + 4;
+  const uint64_t cap_rows = filter ? std::max<uint64_t>(1, n_rows / 2) : 0;
+  Scratch pass_scr(filter ? pass_words * 4 + 16 + size_t(n_wtiles) * 4 + 16 : 0, s);
+  Scratch comp_scr(filter ? cap_rows * 4 + 256 + (l2 ? cap_rows * 4 + 256 : 0) + cap_rows * DIM * 2 : 0, s);
   Scratch kidx_holder;
-  if (row_offset % 32 == 0) {
-    const DevBitmap b = make_dev(filter, kidx_holder, s);
-    k_pass_words<<<div_up(pass_words, 256), 256, 0, s>>>(b, row_offset, n_rows, pass, pass_words);
+  if (!filter) {
+    k_plan<<<1, 32, 0, s>>>(nullptr, uint32_t(n_rows), slices, slices * EPI_PARTS, k, spec_capable,
+                            spec_override, tiles_override, plan);
   } else {
-    const cu_roaring::GpuRoaringView v =
-        cu_roaring::make_view(*reinterpret_cast<const cu_roaring::GpuRoaring*>(filter));
-    const uint64_t threads = pass_words * 32;
-    const int grid = static_cast<int>(std::min<uint64_t>(div_up(threads, 256), uint64_t(sm_count()) * 16));
-    k_pass_bits<<<grid, 256, 0, s>>>(v, row_offset, n_rows, pass, pass_words, filter->universe_size);
+    uint32_t* pass = pass_scr.as<uint32_t>();
+    uint32_t* d_total = pass + pass_words;
+    uint32_t* tiles = d_total + 4;
+    if (row_offset % 32 == 0) {
+      const DevBitmap b = make_dev(filter, kidx_holder, s);
+      k_pass_words<<<div_up(pass_words, 256), 256, 0, s>>>(b, row_offset, n_rows, pass, pass_words);
+    } else {
+      const cu_roaring::GpuRoaringView v =
+          cu_roaring::make_view(*reinterpret_cast<const cu_roaring::GpuRoaring*>(filter));
+      const uint64_t threads = pass_words * 32;
+      const int grid = static_cast<int>(std::min<uint64_t>(div_up(threads, 256), uint64_t(sm_count()) * 16));
+      k_pass_bits<<<grid, 256, 0, s>>>(v, row_offset, n_rows, pass, pass_words, filter->universe_size);
+    }
+    k_pass_tile_sums<<<n_wtiles, kWordTile, 0, s>>>(pass, pass_words, tiles, count);
+    CR_CUDA(cudaGetLastError());
+    tr.mark("pass_bits", s);
+    // Pre-filter below half density: compact the passing rows' indices (and
+    // norms) and copy those rows into a dense block searched with TMA tiles.
+    uint32_t* idx = comp_scr.as<uint32_t>();
+    float* comp_norms = l2 ? reinterpret_cast<float*>(
+        (reinterpret_cast<uintptr_t>(idx + cap_rows) + 255) & ~uintptr_t(255)) : nullptr;
+    uint16_t* comp = reinterpret_cast<uint16_t*>(
+        (reinterpret_cast<uintptr_t>(l2 ? static_cast<void*>(comp_norms + cap_rows)
+                                        : static_cast<void*>(idx + cap_rows)) + 255) & ~uintptr_t(255));
+    {
+      ProfileScope prof_c(CR_KERNEL_TOPK_COMPACT, s);
+      k_pass_compact<<<n_wtiles, kWordTile, 0, s>>>(pass, pass_words, tiles, n_wtiles, idx, d_total,
+                                                    l2 ? norms : nullptr, comp_norms,
+                                                    reinterpret_cast<const uint4*>(d_db),
+                                                    reinterpret_cast<uint4*>(comp), uint32_t(cap_rows));
+      CR_CUDA(cudaGetLastError());
+    }
+    k_plan<<<1, 32, 0, s>>>(count, uint32_t(n_rows), slices, slices * EPI_PARTS, k, spec_capable, spec_override,
+                            tiles_override, plan);
+    tr.mark("compact_gather", s);
+    in.pass = pass;
+    in.comp = comp;
+    in.comp_cap = cap_rows;
+    in.comp_norms = comp_norms;
+    in.idx = idx;
   }
-  CR_CUDA(cudaMemsetAsync(d_total + 1, 0, 4, s));
-  k_pass_tile_sums<<<n_wtiles, kWordTile, 0, s>>>(pass, pass_words, tiles, d_total + 1);
   CR_CUDA(cudaGetLastError());
-  // Count first: the compacted copy is only worth it below half density.
-  tr.mark("pass_bits", s);
-  uint32_t* h_word = pinned_words();
-  CR_CUDA(cudaMemcpyAsync(h_word, d_total + 1, 4, cudaMemcpyDeviceToHost, s));
-  CR_CUDA(cudaStreamSynchronize(s));
-  const uint32_t n_pass = h_word[0];
-  if (n_pass == 0) {
-    const uint64_t n = uint64_t(n_queries) * k;
-    k_fill_empty<<<div_up(n, 256), 256, 0, s>>>(d_out_dist, d_out_ids, n, l2 ? INFINITY : -INFINITY);
-    CR_CUDA(cudaGetLastError());
-    return CR_OK;
-  }
-  if (uint64_t(n_pass) * 2 > n_rows) {
-    // Dense rows with the predicate applied per 32-row chunk in the epilogue.
-    run_topk_core(d_db, norms, n_rows, pass, nullptr, d_queries, n_queries, row_offset, k, metric,
-                  d_out_dist, d_out_ids, s);
-    return CR_OK;
-  }
-  // Pre-filter: compact the passing rows' indices (and norms), copy those
-  // rows into a dense block and search it with TMA tiles.
-  Scratch comp_scr(size_t(n_pass) * 4 + 256 + (l2 ? size_t(n_pass) * 4 + 256 : 0) + size_t(n_pass) * DIM * 2, s);
-  uint32_t* idx = comp_scr.as<uint32_t>();
-  float* comp_norms = l2 ? reinterpret_cast<float*>(
-      (reinterpret_cast<uintptr_t>(idx + n_pass) + 255) & ~uintptr_t(255)) : nullptr;
-  uint16_t* comp = reinterpret_cast<uint16_t*>(
-      (reinterpret_cast<uintptr_t>(l2 ? static_cast<void*>(comp_norms + n_pass) : static_cast<void*>(idx + n_pass)) +
-       255) & ~uintptr_t(255));
-  {
-    tr.mark("count_sync", s);
-    ProfileScope prof_c(CR_KERNEL_TOPK_COMPACT, s);
-    k_pass_compact<<<n_wtiles, kWordTile, 0, s>>>(pass, pass_words, tiles, n_wtiles, idx, d_total,
-                                                  l2 ? norms : nullptr, comp_norms,
-                                                  reinterpret_cast<const uint4*>(d_db), reinterpret_cast<uint4*>(comp));
-    CR_CUDA(cudaGetLastError());
-  }
-  tr.mark("compact_gather", s);
-  run_topk_core(comp, comp_norms, n_pass, nullptr, idx, d_queries, n_queries, row_offset, k, metric,
-                d_out_dist, d_out_ids, s);
+  bool appended = false, unused = false;
+  run_search(in, d_queries, n_queries, row_offset, k, metric, d_out_dist, d_out_ids, s, true, true, nullptr, err0,
+             &appended);
+  // The exact redo with per-list merging, which needs neither candidate
+  // capacity nor a speculative bound: every kernel of it returns at once
+  // unless the first search flagged an overflowing candidate array
+  // (degenerate score distributions, e.g. massive ties) or a speculative
+  // bound above some query's k-th best.
+  if (appended)
+    run_search(in, d_queries, n_queries, row_offset, k, metric, d_out_dist, d_out_ids, s, false, false, err0, err1,
+               &unused);
+  ErrorRing::get().record(err0, appended ? err1 : nullptr, s);
   tr.mark("search", s);
   tr.print();
+  CR_API_END
+}
+
+extern "C" int cr_filtered_topk_check(void)
+{
+  CR_API_BEGIN
+  ErrorRing::get().check(true);
   CR_API_END
 }
 

@@ -35,7 +35,7 @@ EXPORTED_SYMBOLS = (
     "cr_promote_auto", "cr_deep_copy", "cr_set_operation", "cr_multi_and", "cr_multi_or",
     "cr_decompress_to_bitset", "cr_decompress_to_bitset_alloc", "cr_enumerate_ids_i64",
     "cr_enumerate_ids_u32", "cr_enumerate_ids_alloc", "cr_enumerate_ids_u32_noalloc", "cr_contains_batch", "cr_filtered_topk",
-    "cr_row_norms", "cr_topk_merge", "cr_profile_enable", "cr_profile_last_ms", "cr_profile_sum_ms",
+    "cr_row_norms", "cr_topk_merge", "cr_filtered_topk_check", "cr_profile_enable", "cr_profile_last_ms", "cr_profile_sum_ms",
 )
 
 
@@ -85,6 +85,7 @@ _sigs = {
     "cr_topk_merge": ([_vp, _vp, _u32, _u32, _u32, _i32, _vp, _vp, _vp], _i32),
     "cr_profile_enable": ([_i32], _i32),
     "cr_profile_last_ms": ([_i32, C.POINTER(C.c_float)], _i32),
+    "cr_filtered_topk_check": ([], _i32),
     "cr_profile_sum_ms": ([_i32, C.POINTER(C.c_float), C.POINTER(C.c_uint32)], _i32),
 }
 for _name, (_args, _res) in _sigs.items():

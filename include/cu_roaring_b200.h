@@ -190,11 +190,22 @@ int cr_contains_batch(const cr_gpu_roaring* bm, const uint32_t* d_ids, uint64_t 
  *   k         1..256
  *   d_out_dist fp32 [n_queries x k], best first (IP: scores, L2: distances)
  *   d_out_ids  int64 [n_queries x k], -1 where fewer than k rows pass
- * Scratch is allocated stream-ordered on `stream`. */
+ * Stream-ordered: the call returns without waiting for the device (the
+ * search plan, including the pre-filter's choice between compacted and
+ * masked rows, is made on the device, and the exact redo for degenerate
+ * score distributions is queued behind the first pass and skipped by the
+ * device unless needed). Scratch is allocated stream-ordered on `stream`.
+ * A device-side failure (a bounded pipeline wait that ran out) is reported
+ * by the next cr_filtered_topk call on the same host thread or by
+ * cr_filtered_topk_check. */
 int cr_filtered_topk(const uint16_t* d_db, const float* d_db_norms, uint64_t n_rows,
                      uint32_t dim, const uint16_t* d_queries, uint32_t n_queries,
                      const cr_gpu_roaring* filter, uint64_t row_offset, uint32_t k,
                      int metric, float* d_out_dist, int64_t* d_out_ids, cr_stream_t stream);
+
+/* Waits for this host thread's outstanding cr_filtered_topk searches and
+ * returns CR_ERR_DEVICE if any of them failed on the device. */
+int cr_filtered_topk_check(void);
 
 /* Squared L2 norms of fp16 rows (fp32 accumulate) for the L2 metric. */
 int cr_row_norms(const uint16_t* d_db, uint64_t n_rows, uint32_t dim, float* d_out,
