@@ -469,16 +469,18 @@ def main():
     q_host = queries.cpu().pin_memory()
     stream = torch.cuda.current_stream()
 
-    gather_d = torch.empty((world, N_QUERIES, K), dtype=torch.float32, device=dev)
-    gather_i = torch.empty((world, N_QUERIES, K), dtype=torch.int64, device=dev)
+    # Each shard's top-k lands in one packed block (distances then ids), so one
+    # NCCL all-gather carries it; rank 0 merges the gathered blocks in place.
+    block, block_d, block_i = cr.topk_packed_buffer(N_QUERIES, K, dev)
+    gathered = torch.empty((world, block.numel()), dtype=torch.uint8, device=dev)
 
     def step(qdev):
-        d, i = cr.filtered_topk(db, qdev, K, metric=cr.METRIC_IP, filter=filt, row_offset=lo, stream=stream)
+        d, i = cr.filtered_topk(db, qdev, K, metric=cr.METRIC_IP, filter=filt, row_offset=lo, stream=stream,
+                                out_dist=block_d, out_ids=block_i)
         if world > 1:
-            dist.all_gather_into_tensor(gather_d, d)
-            dist.all_gather_into_tensor(gather_i, i)
+            dist.all_gather_into_tensor(gathered, block)
             if rank == 0:
-                d, i = cr.topk_merge(gather_d, gather_i, K, metric=cr.METRIC_IP, stream=stream)
+                d, i = cr.topk_merge_packed(gathered, N_QUERIES, K, metric=cr.METRIC_IP, stream=stream)
         return d, i
 
     # device-resident value
@@ -590,7 +592,11 @@ def main():
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "queries/s", "h2d_bytes_per_step": N_QUERIES * DIM * 2,
                     "d2h_bytes_per_step": N_QUERIES * K * 12},
-            "gpu_launches": args.steps * ((6 if 2 * pass_local <= rows_local else 4) + (1 if world > 1 else 0)),
+            # per step: k_pass_words, k_pass_tile_sums, k_pass_compact, k_plan,
+            # k_topk (prologue), k_spec, k_topk (main), k_merge, and the
+            # guarded exact redo's k_topk + k_merge (exit at once unless
+            # needed); with N > 1 rank 0's k_merge of the gathered blocks
+            "gpu_launches": args.steps * (10 + (1 if world > 1 else 0)),
             "clocks": clocks.summary(),
         }
         if secondary:

@@ -744,7 +744,8 @@ __global__ void __launch_bounds__(MERGE_THREADS) k_merge(const float* part_s, co
                                                          const uint32_t* pub, uint32_t n_lists,
                                                          uint32_t n_rows, const uint32_t* spec_used,
                                                          uint32_t* err, const SearchPlan* plan,
-                                                         const uint32_t* guard)
+                                                         const uint32_t* guard, uint64_t s_stride,
+                                                         uint64_t i_stride)
 {
   if (guard && !(*reinterpret_cast<const volatile uint32_t*>(guard) & (kErrOverflow | kErrSpec))) return;
   if (plan) {  // a search's candidates: rows and row ids as the plan decided
@@ -811,9 +812,9 @@ __global__ void __launch_bounds__(MERGE_THREADS) k_merge(const float* part_s, co
       }
     } else if (c < total) {
       const uint32_t pidx = static_cast<uint32_t>(c / k), e = static_cast<uint32_t>(c % k);
-      const size_t g = (size_t(pidx) * n_queries + q) * k + e;
-      i = part_id[g];
-      const float x = part_s[g];
+      const size_t g = size_t(q) * k + e;
+      i = part_id[pidx * i_stride + g];
+      const float x = part_s[pidx * s_stride + g];
       v = (i < 0) ? -INFINITY : (kind == 0 ? x : (l2 ? -x : x));
     }
     s[slot] = v;
@@ -1012,10 +1013,10 @@ __global__ void __launch_bounds__(MERGE_THREADS) k_merge(const float* part_s, co
       __syncthreads();
       for (uint32_t c = threadIdx.x; c < total; c += MERGE_THREADS) {
         const uint32_t pidx = c / k, e = c % k;
-        const size_t g = (size_t(pidx) * n_queries + q) * k + e;
-        const int64_t i = part_id[g];
+        const size_t g = size_t(q) * k + e;
+        const int64_t i = part_id[pidx * i_stride + g];
         if (i >= 0) {
-          const float x = part_s[g];
+          const float x = part_s[pidx * s_stride + g];
           const uint32_t slot = atomicAdd(&s_m, 1u);
           s[slot] = kind == 0 ? x : (l2 ? -x : x);
           id[slot] = i;
@@ -1256,8 +1257,13 @@ void merge_launch(const float* ps, const int64_t* pid, uint32_t parts, uint32_t 
                   const uint32_t* cand_r = nullptr, const uint32_t* row_map = nullptr,
                   uint64_t row_offset = 0, const uint32_t* pub = nullptr, uint32_t n_lists = 0,
                   uint32_t n_rows = 0, const uint32_t* spec_used = nullptr, uint32_t* err = nullptr,
-                  const SearchPlan* plan = nullptr, const uint32_t* guard = nullptr)
+                  const SearchPlan* plan = nullptr, const uint32_t* guard = nullptr, uint64_t s_stride = 0,
+                  uint64_t i_stride = 0)
 {
+  // Lists of part p: scores at ps + p * s_stride, ids at pid + p * i_stride
+  // (elements; default: parts packed back to back as [parts][nq][k]).
+  if (!s_stride) s_stride = uint64_t(nq) * k;
+  if (!i_stride) i_stride = uint64_t(nq) * k;
   static std::once_flag once;
   const size_t smem = MERGE_N * 12;
   std::call_once(once, [&] {
@@ -1266,7 +1272,7 @@ void merge_launch(const float* ps, const int64_t* pid, uint32_t parts, uint32_t 
   ProfileScope prof(CR_KERNEL_TOPK_MERGE, s);
   k_merge<<<nq, MERGE_THREADS, smem, s>>>(ps, pid, parts, nq, k, metric, kind, queries, dim, od, oi,
                                           cand_cnt, cap, cand_r, row_map, row_offset, pub, n_lists, n_rows,
-                                          spec_used, err, plan, guard);
+                                          spec_used, err, plan, guard, s_stride, i_stride);
   CR_CUDA(cudaGetLastError());
 }
 
@@ -1636,6 +1642,25 @@ extern "C" int cr_filtered_topk(const uint16_t* d_db, const float* d_db_norms, u
   ErrorRing::get().record(err0, appended ? err1 : nullptr, s);
   tr.mark("search", s);
   tr.print();
+  CR_API_END
+}
+
+extern "C" int cr_topk_merge_packed(const void* d_parts, uint64_t part_bytes, uint32_t n_parts,
+                                    uint32_t n_queries, uint32_t k, int metric, float* d_out_dist,
+                                    int64_t* d_out_ids, cr_stream_t stream)
+{
+  CR_API_BEGIN
+  CR_REQUIRE(d_parts && d_out_dist && d_out_ids, "cr_topk_merge_packed: null buffer");
+  CR_REQUIRE(k >= 1 && k <= 256 && n_parts >= 1, "cr_topk_merge_packed: bad k or n_parts");
+  const uint64_t dist_bytes = uint64_t(n_queries) * k * 4;
+  CR_REQUIRE(part_bytes % 8 == 0 && dist_bytes % 8 == 0 && part_bytes >= dist_bytes * 3,
+             "cr_topk_merge_packed: each part needs 8-byte aligned dist and id blocks (n_queries * k even)");
+  CR_REQUIRE((reinterpret_cast<uintptr_t>(d_parts) & 7u) == 0, "cr_topk_merge_packed: d_parts must be 8-byte aligned");
+  const char* base = static_cast<const char*>(d_parts);
+  merge_launch(reinterpret_cast<const float*>(base), reinterpret_cast<const int64_t*>(base + dist_bytes), n_parts,
+               n_queries, k, metric, 1, nullptr, 0, d_out_dist, d_out_ids, reinterpret_cast<cudaStream_t>(stream),
+               nullptr, 0, nullptr, nullptr, 0, nullptr, 0, 0, nullptr, nullptr, nullptr, nullptr, part_bytes / 4,
+               part_bytes / 8);
   CR_API_END
 }
 

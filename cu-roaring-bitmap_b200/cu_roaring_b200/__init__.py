@@ -35,7 +35,7 @@ EXPORTED_SYMBOLS = (
     "cr_promote_auto", "cr_deep_copy", "cr_set_operation", "cr_multi_and", "cr_multi_or",
     "cr_decompress_to_bitset", "cr_decompress_to_bitset_alloc", "cr_enumerate_ids_i64",
     "cr_enumerate_ids_u32", "cr_enumerate_ids_alloc", "cr_enumerate_ids_u32_noalloc", "cr_contains_batch", "cr_filtered_topk",
-    "cr_row_norms", "cr_topk_merge", "cr_filtered_topk_check", "cr_profile_enable", "cr_profile_last_ms", "cr_profile_sum_ms",
+    "cr_row_norms", "cr_topk_merge", "cr_topk_merge_packed", "cr_filtered_topk_check", "cr_profile_enable", "cr_profile_last_ms", "cr_profile_sum_ms",
 )
 
 
@@ -85,6 +85,8 @@ _sigs = {
     "cr_topk_merge": ([_vp, _vp, _u32, _u32, _u32, _i32, _vp, _vp, _vp], _i32),
     "cr_profile_enable": ([_i32], _i32),
     "cr_profile_last_ms": ([_i32, C.POINTER(C.c_float)], _i32),
+    "cr_topk_merge_packed": ([C.c_void_p, C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, _i32, C.c_void_p,
+                              C.c_void_p, C.c_void_p], _i32),
     "cr_filtered_topk_check": ([], _i32),
     "cr_profile_sum_ms": ([_i32, C.POINTER(C.c_float), C.POINTER(C.c_uint32)], _i32),
 }
@@ -378,6 +380,31 @@ def topk_merge(dist_parts, id_parts, k: int, metric: int = METRIC_IP, stream=Non
     out_i = torch.empty((q, k), dtype=torch.int64, device=dist_parts.device)
     _check(_lib.cr_topk_merge(_dev_ptr(dist_parts), _dev_ptr(id_parts), p, q, k, metric, _dev_ptr(out_d),
                               _dev_ptr(out_i), _stream_ptr(stream)), "topk_merge")
+    return out_d, out_i
+
+
+def topk_packed_buffer(n_queries: int, k: int, device):
+    """A send block for one shard's top-k: (block, dist view, ids view). Pass
+    the views as filtered_topk's out_dist / out_ids, gather the blocks with one
+    collective, and merge them with topk_merge_packed."""
+    torch = _torch()
+    if (n_queries * k) % 2:
+        raise ValueError("n_queries * k must be even for the packed layout")
+    nd = n_queries * k
+    block = torch.empty(nd * 12, dtype=torch.uint8, device=device)
+    dist = block[: nd * 4].view(torch.float32).view(n_queries, k)
+    ids = block[nd * 4:].view(torch.int64).view(n_queries, k)
+    return block, dist, ids
+
+
+def topk_merge_packed(blocks, n_queries: int, k: int, metric: int = METRIC_IP, stream=None):
+    """Merge [parts, 12 * n_queries * k] uint8 blocks (see topk_packed_buffer)."""
+    torch = _torch()
+    p = blocks.shape[0]
+    out_d = torch.empty((n_queries, k), dtype=torch.float32, device=blocks.device)
+    out_i = torch.empty((n_queries, k), dtype=torch.int64, device=blocks.device)
+    _check(_lib.cr_topk_merge_packed(_dev_ptr(blocks), blocks.stride(0), p, n_queries, k, metric,
+                                     _dev_ptr(out_d), _dev_ptr(out_i), _stream_ptr(stream)), "topk_merge_packed")
     return out_d, out_i
 
 

@@ -203,6 +203,15 @@ int cr_filtered_topk(const uint16_t* d_db, const float* d_db_norms, uint64_t n_r
                      const cr_gpu_roaring* filter, uint64_t row_offset, uint32_t k,
                      int metric, float* d_out_dist, int64_t* d_out_ids, cr_stream_t stream);
 
+/* cr_topk_merge over parts that each sit in one packed block, as a single
+ * collective (e.g. an NCCL all-gather of each shard's block) leaves them:
+ * part p starts at (char*)d_parts + p * part_bytes and holds fp32 distances
+ * [n_queries x k] followed by int64 ids [n_queries x k] (n_queries * k even,
+ * part_bytes a multiple of 8 and >= 12 * n_queries * k). No reference
+ * counterpart (the reference has no multi-GPU path). */
+int cr_topk_merge_packed(const void* d_parts, uint64_t part_bytes, uint32_t n_parts, uint32_t n_queries,
+                         uint32_t k, int metric, float* d_out_dist, int64_t* d_out_ids, cr_stream_t stream);
+
 /* Waits for this host thread's outstanding cr_filtered_topk searches and
  * returns CR_ERR_DEVICE if any of them failed on the device. */
 int cr_filtered_topk_check(void);

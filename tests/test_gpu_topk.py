@@ -221,3 +221,21 @@ def test_topk_speculative_bound_verified(cr, oracle, torch_, monkeypatch, spec_j
                                 filter=filt)
         check_topk(d.cpu().numpy(), i.cpu().numpy(), d_ref, i_ref, metric)
     filt.free()
+
+
+def test_topk_merge_packed(cr, oracle, torch_):
+    """Two shards' results written into packed blocks (distances then ids, as
+    one collective would carry them) and merged in place."""
+    n, q, k = 30000, 64, 50
+    db, qs = make_data(n, q, seed=19)
+    dq = torch_.from_numpy(qs).cuda()
+    for metric in (0, 1):
+        d_ref, i_ref = oracle.topk(db, qs, k, metric, None)
+        blocks = []
+        for lo, hi in ((0, 17000), (17000, n)):
+            block, bd, bi = cr.topk_packed_buffer(q, k, "cuda")
+            ddb = torch_.from_numpy(np.ascontiguousarray(db[lo:hi])).cuda()
+            cr.filtered_topk(ddb, dq, k, metric=metric, row_offset=lo, out_dist=bd, out_ids=bi)
+            blocks.append(block)
+        d, i = cr.topk_merge_packed(torch_.stack(blocks), q, k, metric=metric)
+        check_topk(d.cpu().numpy(), i.cpu().numpy(), d_ref, i_ref, metric)
