@@ -1143,7 +1143,7 @@ __global__ void k_row_norms(const uint4* db, uint64_t n_rows, float* out)
 }
 
 // -------------------------------------------------- pre-filter compaction
-constexpr uint32_t kWordTile = 1024;
+constexpr uint32_t kWordTile = 256;  // pass words per block of the count and compaction kernels
 
 __global__ void __launch_bounds__(kWordTile) k_pass_tile_sums(const uint32_t* pass, uint64_t n_words,
                                                               uint32_t* tile_sums, uint32_t* total)
@@ -1164,7 +1164,8 @@ __global__ void __launch_bounds__(kWordTile) k_pass_tile_sums(const uint32_t* pa
 // With `comp`, the block then copies its rows: comp[i] = db[idx[i]]
 // (16 threads x 16 B per 128-dim row), so the gather needs no launch of its
 // own and starts as soon as the block's indices are known.
-__global__ void __launch_bounds__(kWordTile) k_pass_compact(const uint32_t* pass, uint64_t n_words,
+constexpr uint32_t kCompactThreads = 1024;  // threads past the word tile only copy rows
+__global__ void __launch_bounds__(kCompactThreads) k_pass_compact(const uint32_t* pass, uint64_t n_words,
                                                             const uint32_t* tile_sums, uint32_t n_tiles,
                                                             uint32_t* idx, uint32_t* total,
                                                             const float* norms, float* comp_norms,
@@ -1173,19 +1174,19 @@ __global__ void __launch_bounds__(kWordTile) k_pass_compact(const uint32_t* pass
   __shared__ uint32_t s_red[32];
   // Rows of the earlier word tiles: the block's first output slot.
   uint32_t before = 0, all = 0;
-  for (uint32_t j = threadIdx.x; j < n_tiles; j += kWordTile) {
+  for (uint32_t j = threadIdx.x; j < n_tiles; j += kCompactThreads) {
     const uint32_t c = tile_sums[j];
     if (j < blockIdx.x) before += c;
     all += c;
   }
-  const uint32_t base = block_sum<kWordTile>(before, s_red);
-  const uint32_t everything = block_sum<kWordTile>(all, s_red);
+  const uint32_t base = block_sum<kCompactThreads>(before, s_red);
+  const uint32_t everything = block_sum<kCompactThreads>(all, s_red);
   if (blockIdx.x == 0 && threadIdx.x == 0) *total = everything;
   if (everything > cap_rows) return;  // dense plan: the shard is searched with the bitset
   const uint64_t w = uint64_t(blockIdx.x) * kWordTile + threadIdx.x;
-  uint32_t x = w < n_words ? pass[w] : 0u;
+  uint32_t x = (threadIdx.x < kWordTile && w < n_words) ? pass[w] : 0u;
   uint32_t tot;
-  uint32_t pos = base + block_exclusive_scan<kWordTile>(uint32_t(__popc(x)), s_red, &tot);
+  uint32_t pos = base + block_exclusive_scan<kCompactThreads>(uint32_t(__popc(x)), s_red, &tot);
   while (x) {
     const uint32_t r = uint32_t(w * 32 + __ffs(x) - 1);
     idx[pos] = r;
@@ -1197,12 +1198,12 @@ __global__ void __launch_bounds__(kWordTile) k_pass_compact(const uint32_t* pass
   __syncthreads();  // the block's idx[] entries are visible to all its threads
   const uint32_t n16 = tot * 16;
   constexpr uint32_t U = 4;  // independent row loads in flight per thread
-  for (uint32_t i0 = 0; i0 < n16; i0 += kWordTile * U) {
+  for (uint32_t i0 = 0; i0 < n16; i0 += kCompactThreads * U) {
     uint4 v[U];
     uint32_t dst[U];
 #pragma unroll
     for (uint32_t u = 0; u < U; ++u) {
-      const uint32_t i = i0 + u * kWordTile + threadIdx.x;
+      const uint32_t i = i0 + u * kCompactThreads + threadIdx.x;
       dst[u] = i < n16 ? base * 16 + i : 0xFFFFFFFFu;
       if (i < n16) v[u] = __ldcs(db + uint64_t(idx[base + i / 16]) * 16 + (i & 15));
     }
@@ -1612,7 +1613,7 @@ extern "C" int cr_filtered_topk(const uint16_t* d_db, const float* d_db_norms, u
                                         : static_cast<void*>(idx + cap_rows)) + 255) & ~uintptr_t(255));
     {
       ProfileScope prof_c(CR_KERNEL_TOPK_COMPACT, s);
-      k_pass_compact<<<n_wtiles, kWordTile, 0, s>>>(pass, pass_words, tiles, n_wtiles, idx, d_total,
+      k_pass_compact<<<n_wtiles, kCompactThreads, 0, s>>>(pass, pass_words, tiles, n_wtiles, idx, d_total,
                                                     l2 ? norms : nullptr, comp_norms,
                                                     reinterpret_cast<const uint4*>(d_db),
                                                     reinterpret_cast<uint4*>(comp), uint32_t(cap_rows));
