@@ -47,12 +47,14 @@ def build_lib(force: bool = False) -> Path:
         obj = OBJ / (src.stem + ".o")
         objs.append(obj)
         if force or not obj.exists() or obj.stat().st_mtime < max(src.stat().st_mtime, hdr_time):
-            jobs.append([NVCC, *ARCH, *FLAGS, "-c", str(src), "-o", str(obj)])
+            # topk.cu launches its exact redo from the device (relocatable device code)
+            rdc = ["-rdc=true"] if src.stem == "topk" else []
+            jobs.append([NVCC, *ARCH, *FLAGS, *rdc, "-c", str(src), "-o", str(obj)])
     with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
         list(ex.map(_run, jobs))
     if force or jobs or not LIB.exists() or LIB.stat().st_mtime < _newest(objs):
-        _run([NVCC, *ARCH, "-shared", "--cudart", "shared", "-o", str(LIB), *map(str, objs),
-              "-Xlinker", "-rpath,/usr/local/cuda/lib64"])
+        _run([NVCC, *ARCH, "-shared", "-rdc=true", "--cudart", "shared", "-o", str(LIB), *map(str, objs),
+              "-lcudadevrt", "-Xlinker", "-rpath,/usr/local/cuda/lib64"])
     return LIB
 
 

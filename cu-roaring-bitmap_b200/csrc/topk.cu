@@ -121,6 +121,7 @@ struct TopkParams {
 
 constexpr uint32_t kErrOverflow = 64u;  // a candidate array filled up (append mode)
 constexpr uint32_t kErrSpec = 128u;      // a query's speculative bound was above its k-th best
+constexpr uint32_t kErrLaunch = 256u;    // the device could not launch the exact redo
 constexpr uint32_t kPrologueTiles = 4;  // publish-only tiles at the start of each slice (append mode)
 
 // Order-preserving map float -> uint32 (larger float -> larger key); 0 is
@@ -733,7 +734,7 @@ __device__ void bitonic_sort(float* s, int64_t* id, uint32_t n = MERGE_N)
 
 // One CTA per query: the best k of `parts` sorted lists. kind 0: inputs are
 // internal scores of k_topk; kind 1: inputs are final distances.
-__global__ void __launch_bounds__(MERGE_THREADS) k_merge(const float* part_s, const int64_t* part_id,
+__global__ void __launch_bounds__(MERGE_THREADS, 3) k_merge(const float* part_s, const int64_t* part_id,
                                                          uint32_t parts, uint32_t n_queries,
                                                          uint32_t k, int metric, int kind,
                                                          const __half* queries, uint32_t dim,
@@ -1277,6 +1278,31 @@ void merge_launch(const float* ps, const int64_t* pid, uint32_t parts, uint32_t 
   CR_CUDA(cudaGetLastError());
 }
 
+// The exact redo (per-list merging: no candidate capacity, no speculative
+// bound) launched from the device, and only when the first pass flagged an
+// overflowing candidate array or a speculative bound above some query's k-th
+// best: one block checks the flag, zeroes the redo's counters and tail-launches
+// the search and its merge (they run, in order, once this block has finished).
+__global__ void __launch_bounds__(1024) k_redo_gate(const uint32_t* guard, uint32_t* zero, uint64_t zero_words,
+                                                    uint32_t* err, dim3 grid, const __grid_constant__ CUtensorMap tq,
+                                                    const __grid_constant__ CUtensorMap tdb,
+                                                    const __grid_constant__ CUtensorMap tcomp, TopkParams tp,
+                                                    uint32_t n_lists, const __half* queries, float* out_d,
+                                                    int64_t* out_id)
+{
+  if (!(*reinterpret_cast<const volatile uint32_t*>(guard) & (kErrOverflow | kErrSpec))) return;
+  for (uint64_t i = threadIdx.x; i < zero_words; i += blockDim.x) zero[i] = 0u;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    k_topk<false><<<grid, THREADS, SMEM_TOTAL, cudaStreamTailLaunch>>>(tq, tdb, tcomp, tp);
+    const uint64_t stride = uint64_t(tp.n_queries) * tp.k;
+    k_merge<<<tp.n_queries, MERGE_THREADS, MERGE_N * 12, cudaStreamTailLaunch>>>(
+        tp.part_s, tp.part_id, n_lists, tp.n_queries, tp.k, tp.metric, 0, queries, DIM, out_d, out_id, nullptr, 0,
+        nullptr, nullptr, 0, nullptr, 0, 0, nullptr, err, nullptr, nullptr, stride, stride);
+    if (cudaGetLastError() != cudaSuccess) atomicOr(err, kErrLaunch);
+  }
+}
+
 void row_norms(const uint16_t* db, uint64_t n_rows, float* out, cudaStream_t s)
 {
   const uint64_t threads = n_rows * 16;
@@ -1406,7 +1432,8 @@ struct SearchInput {
 // One search over the planned rows plus the per-query merge, stream-ordered.
 // Append mode (candidate arrays, speculative bound) unless disabled; `guard`
 // makes every kernel of it a no-op unless that error word asks for a redo;
-// device-side failures land in `err` (16 bytes, zeroed here).
+// device-side failures land in `err` (16 bytes, zeroed by the caller). With
+// a guard the search is the exact redo, launched by k_redo_gate.
 static void run_search(const SearchInput& in, const uint16_t* d_queries, uint32_t n_queries, uint64_t row_offset,
                        uint32_t k, int metric, float* d_out_dist, int64_t* d_out_ids, cudaStream_t s,
                        bool allow_append, bool allow_spec, const uint32_t* guard, uint32_t* err,
@@ -1450,8 +1477,7 @@ static void run_search(const SearchInput& in, const uint16_t* d_queries, uint32_
   tp.pub = reinterpret_cast<uint32_t*>(p); p += pub_b;
   if (append) { tp.cand_cnt = reinterpret_cast<uint32_t*>(p); p += cnt_b; }
   if (spec_capable) { tp.pub_top = reinterpret_cast<uint32_t*>(p); p += top_b; }
-  CR_CUDA(cudaMemsetAsync(err, 0, 16, s));
-  CR_CUDA(cudaMemsetAsync(tp.shared_thr, 0, zero_b, s));
+  if (!guard) CR_CUDA(cudaMemsetAsync(tp.shared_thr, 0, zero_b, s));
   p = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(p) + 255) & ~uintptr_t(255));
   tp.n_queries = n_queries;
   tp.k = k;
@@ -1489,6 +1515,13 @@ static void run_search(const SearchInput& in, const uint16_t* d_queries, uint32_
   const CUtensorMap tdb = make_map(in.db, in.shard_rows, BN);
   const CUtensorMap tcomp = in.comp ? make_map(in.comp, std::max<uint64_t>(1, in.comp_cap), BN) : tdb;
   const dim3 grid(qtiles, slices);
+  if (guard) {
+    k_redo_gate<<<1, 1024, 0, s>>>(guard, tp.shared_thr, zero_b / 4, err, grid, tq, tdb, tcomp, tp, n_lists,
+                                   reinterpret_cast<const __half*>(d_queries), d_out_dist, d_out_ids);
+    CR_CUDA(cudaGetLastError());
+    Trace::get().mark("redo_gate", s);
+    return;
+  }
   {
     ProfileScope prof(guard ? -1 : CR_KERNEL_TOPK, s);
     if (spec_capable) {
@@ -1554,7 +1587,7 @@ extern "C" int cr_filtered_topk(const uint16_t* d_db, const float* d_db_norms, u
   uint32_t* count = reinterpret_cast<uint32_t*>(ctl.as<char>() + 64);
   uint32_t* err0 = reinterpret_cast<uint32_t*>(ctl.as<char>() + 128);
   uint32_t* err1 = reinterpret_cast<uint32_t*>(ctl.as<char>() + 192);
-  CR_CUDA(cudaMemsetAsync(count, 0, 4, s));
+  CR_CUDA(cudaMemsetAsync(ctl.as<char>(), 0, 256, s));
 
   // Squared norms of the shard rows (L2 only), computed here when not given.
   Scratch norm_scr((l2 && !d_db_norms) ? n_rows * 4 : 0, s);
