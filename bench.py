@@ -448,6 +448,14 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and hasattr(os, "sched_setaffinity"):
+        # One disjoint block of host cores per rank: each rank's launches are
+        # host-bound at small shards, and the step waits for the slowest rank.
+        cores = sorted(os.sched_getaffinity(0))
+        per = max(1, len(cores) // int(os.environ.get("LOCAL_WORLD_SIZE", world)))
+        mine = cores[local * per:(local + 1) * per]
+        if mine:
+            os.sched_setaffinity(0, mine)
     torch.cuda.set_device(local)
     dev = "cuda"
     if world > 1:

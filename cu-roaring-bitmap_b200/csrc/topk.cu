@@ -32,6 +32,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <vector>
 
@@ -632,7 +633,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 0) tmem_dealloc(tmem, TMEM_COLS);
 }
 
-// One thread: the search plan from the pass count (`count`, null = every
+// The search plan from the pass count (`count`, null = every
 // shard row passes). Below half density the passing rows are compacted and
 // searched; otherwise the shard is searched with the pass bitset. Then the
 // tiling over `slices`, and the speculative bound's rank: the prologue sees
@@ -641,11 +642,15 @@ __global__ void __launch_bounds__(THREADS, 1)
 // probability P(Poisson(k * sample / rows) >= spec_j), taken below 1e-9
 // (each list's best three only lower the value). spec_override (measurement
 // and tests) forces the rank when >= 0; tiles_override the prologue length.
-__global__ void k_plan(const uint32_t* count, uint32_t shard_rows, uint32_t slices, uint32_t n_lists,
-                       uint32_t k, uint32_t spec_capable, int spec_override, int tiles_override,
-                       SearchPlan* plan)
+struct PlanArgs {
+  uint32_t shard_rows, slices, n_lists, k, spec_capable;
+  int spec_override, tiles_override;
+};
+__device__ void make_plan(const uint32_t* count, const PlanArgs a, SearchPlan* plan)
 {
-  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  const uint32_t shard_rows = a.shard_rows, slices = a.slices, n_lists = a.n_lists, k = a.k;
+  const uint32_t spec_capable = a.spec_capable;
+  const int spec_override = a.spec_override, tiles_override = a.tiles_override;
   SearchPlan pl{};
   const uint32_t n_pass = count ? *count : shard_rows;
   pl.dense = (count == nullptr || uint64_t(n_pass) * 2 > shard_rows) ? 1u : 0u;
@@ -672,6 +677,11 @@ __global__ void k_plan(const uint32_t* count, uint32_t shard_rows, uint32_t slic
     if (spec_override >= 0) pl.spec_j = min(uint32_t(spec_override), 3 * n_lists);
   }
   *plan = pl;
+}
+
+__global__ void k_plan(const uint32_t* count, const PlanArgs a, SearchPlan* plan)
+{
+  if (threadIdx.x == 0 && blockIdx.x == 0) make_plan(count, a, plan);
 }
 
 // One warp per query: spec_used[q] = the j-th largest of the n_vals (<= 256)
@@ -1071,14 +1081,17 @@ __global__ void k_pass_bits(cu_roaring::GpuRoaringView v, uint64_t row_offset, u
 // 32 IDs of a word then share one container): one key lookup per word; a
 // BITMAP container gives the word directly, ARRAY and RUN containers are
 // searched for the word's 32-ID window.
-__global__ void k_pass_words(DevBitmap b, uint64_t row_offset, uint64_t n_rows, uint32_t* out,
-                             uint64_t n_words)
+// 256 threads, one pass word each; the block's popcount lands in
+// tile_sums[block] and is added to *count.
+__global__ void __launch_bounds__(256) k_pass_words(DevBitmap b, uint64_t row_offset, uint64_t n_rows,
+                                                    uint32_t* out, uint64_t n_words, uint32_t* tile_sums,
+                                                    uint32_t* count)
 {
+  __shared__ uint32_t s_red[32];
   const uint64_t w = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (w >= n_words) return;
   const uint64_t id0 = row_offset + w * 32;
   uint32_t bits = 0;
-  if (id0 <= 0xFFFFFFFFull) {
+  if (w < n_words && id0 <= 0xFFFFFFFFull) {
     const uint32_t key = uint32_t(id0 >> 16), low0 = uint32_t(id0 & 0xFFFFu);
     const ContainerRef c = dev_container(b, dev_lookup(b, key));
     if (c.idx >= 0) {
@@ -1119,7 +1132,12 @@ __global__ void k_pass_words(DevBitmap b, uint64_t row_offset, uint64_t n_rows, 
     const uint64_t id = id0 + j;
     if (w * 32 + j >= n_rows || id >= U) bits &= ~(1u << j);
   }
-  out[w] = bits;
+  if (w < n_words) out[w] = bits;
+  const uint32_t t = block_sum<256>(uint32_t(__popc(w < n_words ? bits : 0u)), s_red);
+  if (threadIdx.x == 0) {
+    tile_sums[blockIdx.x] = t;
+    atomicAdd(count, t);
+  }
 }
 
 // Squared norms, 16 lanes per 128-dim row (16 bytes each).
@@ -1170,8 +1188,12 @@ __global__ void __launch_bounds__(kCompactThreads) k_pass_compact(const uint32_t
                                                             const uint32_t* tile_sums, uint32_t n_tiles,
                                                             uint32_t* idx, uint32_t* total,
                                                             const float* norms, float* comp_norms,
-                                                            const uint4* db, uint4* comp, uint32_t cap_rows)
+                                                            const uint4* db, uint4* comp, uint32_t cap_rows,
+                                                            const uint32_t* count, const PlanArgs pa,
+                                                            SearchPlan* plan)
 {
+  // The pass count is final (the count kernel has finished): plan here.
+  if (blockIdx.x == 0 && threadIdx.x == 0) make_plan(count, pa, plan);
   __shared__ uint32_t s_red[32];
   // Rows of the earlier word tiles: the block's first output slot.
   uint32_t before = 0, all = 0;
@@ -1362,6 +1384,44 @@ struct Trace {
 
 // The tcgen05 search over `n_rows` rows (optionally masked by `pass`, row
 // ids optionally translated by `row_map`) plus the per-query merge.
+// Scratch of cr_filtered_topk: chunks of device memory kept per (device,
+// stream, host thread) and handed out again by every call, so a steady stream
+// of searches allocates nothing. Calls on one stream run in stream order, so
+// reusing the memory of the previous call is safe; each host thread has its
+// own chunks. The memory stays allocated until the thread exits.
+struct Arena {
+  struct Chunk { char* p; size_t cap; };
+  std::vector<Chunk> chunks;
+  size_t ci = 0, off = 0;
+  cudaStream_t s = nullptr;
+  static Arena& get(cudaStream_t st)
+  {
+    thread_local std::map<std::pair<int, cudaStream_t>, Arena> arenas;
+    int dev = 0;
+    CR_CUDA(cudaGetDevice(&dev));
+    Arena& a = arenas[{dev, st}];
+    a.s = st;
+    return a;
+  }
+  void reset() { ci = 0; off = 0; }
+  template <class T> T* take(size_t bytes)
+  {
+    if (bytes == 0) return nullptr;
+    bytes = (bytes + 255) & ~size_t(255);
+    for (; ci < chunks.size(); ++ci, off = 0)
+      if (off + bytes <= chunks[ci].cap) {
+        char* r = chunks[ci].p + off;
+        off += bytes;
+        return reinterpret_cast<T*>(r);
+      }
+    const size_t cap = std::max(bytes, size_t(64) << 20);
+    chunks.push_back({static_cast<char*>(dev_alloc(cap, s)), cap});
+    ci = chunks.size() - 1;
+    off = bytes;
+    return reinterpret_cast<T*>(chunks[ci].p);
+  }
+};
+
 // Device-side failures of a search (bounded waits that ran out) are copied to
 // a small ring of page-locked words per host thread and reported by the next
 // call on that thread, or by cr_filtered_topk_check, without making the
@@ -1469,8 +1529,7 @@ static void run_search(const SearchInput& in, const uint16_t* d_queries, uint32_
   // by one memset: per-query shared thresholds, published bounds, candidate
   // counts, published best three.
   const size_t zero_b = size_t(n_queries) * 4 + pub_b + cnt_b + top_b;
-  Scratch scr(zero_b + 256 + list_b * 2 + cbuf_b * 2 + part_b * 12 + cand_b * 2 + spec_b + 256, s);
-  char* p = scr.as<char>();
+  char* p = Arena::get(s).take<char>(zero_b + 256 + list_b * 2 + cbuf_b * 2 + part_b * 12 + cand_b * 2 + spec_b + 256);
   TopkParams tp{};
   tp.err = err;
   tp.shared_thr = reinterpret_cast<uint32_t*>(p); p += size_t(n_queries) * 4;
@@ -1582,19 +1641,21 @@ extern "C" int cr_filtered_topk(const uint16_t* d_db, const float* d_db_norms, u
 
   // Control block for the whole call: plan, pass count, both searches' error
   // words (the fallback reads the first one).
-  Scratch ctl(256, s);
-  SearchPlan* plan = reinterpret_cast<SearchPlan*>(ctl.as<char>());
-  uint32_t* count = reinterpret_cast<uint32_t*>(ctl.as<char>() + 64);
-  uint32_t* err0 = reinterpret_cast<uint32_t*>(ctl.as<char>() + 128);
-  uint32_t* err1 = reinterpret_cast<uint32_t*>(ctl.as<char>() + 192);
-  CR_CUDA(cudaMemsetAsync(ctl.as<char>(), 0, 256, s));
+  Arena& arena = Arena::get(s);
+  arena.reset();
+  char* ctl = arena.take<char>(256);
+  SearchPlan* plan = reinterpret_cast<SearchPlan*>(ctl);
+  uint32_t* count = reinterpret_cast<uint32_t*>(ctl + 64);
+  uint32_t* err0 = reinterpret_cast<uint32_t*>(ctl + 128);
+  uint32_t* err1 = reinterpret_cast<uint32_t*>(ctl + 192);
+  CR_CUDA(cudaMemsetAsync(ctl, 0, 256, s));
 
   // Squared norms of the shard rows (L2 only), computed here when not given.
-  Scratch norm_scr((l2 && !d_db_norms) ? n_rows * 4 : 0, s);
   const float* norms = d_db_norms;
   if (l2 && !norms) {
-    row_norms(d_db, n_rows, norm_scr.as<float>(), s);
-    norms = norm_scr.as<float>();
+    float* nb = arena.take<float>(n_rows * 4);
+    row_norms(d_db, n_rows, nb, s);
+    norms = nb;
   }
   SearchInput in{};
   in.db = d_db;
@@ -1613,47 +1674,42 @@ extern "C" int cr_filtered_topk(const uint16_t* d_db, const float* d_db_norms, u
   const uint64_t pass_words = (n_rows + 31) / 32;
   const uint32_t n_wtiles = div_up(pass_words, kWordTile);
   const uint64_t cap_rows = filter ? std::max<uint64_t>(1, n_rows / 2) : 0;
-  Scratch pass_scr(filter ? pass_words * 4 + 16 + size_t(n_wtiles) * 4 + 16 : 0, s);
-  Scratch comp_scr(filter ? cap_rows * 4 + 256 + (l2 ? cap_rows * 4 + 256 : 0) + cap_rows * DIM * 2 : 0, s);
   Scratch kidx_holder;
+  const PlanArgs pa{uint32_t(n_rows), slices, slices * EPI_PARTS, k, spec_capable, spec_override, tiles_override};
   if (!filter) {
-    k_plan<<<1, 32, 0, s>>>(nullptr, uint32_t(n_rows), slices, slices * EPI_PARTS, k, spec_capable,
-                            spec_override, tiles_override, plan);
+    k_plan<<<1, 32, 0, s>>>(nullptr, pa, plan);
   } else {
-    uint32_t* pass = pass_scr.as<uint32_t>();
-    uint32_t* d_total = pass + pass_words;
-    uint32_t* tiles = d_total + 4;
+    uint32_t* pass = arena.take<uint32_t>(pass_words * 4 + 16);
+    uint32_t* d_total = arena.take<uint32_t>(16);
+    uint32_t* tiles = arena.take<uint32_t>(size_t(n_wtiles) * 4);
     if (row_offset % 32 == 0) {
+      static_assert(kWordTile == 256, "one pass-word block per word tile");
       const DevBitmap b = make_dev(filter, kidx_holder, s);
-      k_pass_words<<<div_up(pass_words, 256), 256, 0, s>>>(b, row_offset, n_rows, pass, pass_words);
+      k_pass_words<<<n_wtiles, 256, 0, s>>>(b, row_offset, n_rows, pass, pass_words, tiles, count);
     } else {
       const cu_roaring::GpuRoaringView v =
           cu_roaring::make_view(*reinterpret_cast<const cu_roaring::GpuRoaring*>(filter));
       const uint64_t threads = pass_words * 32;
       const int grid = static_cast<int>(std::min<uint64_t>(div_up(threads, 256), uint64_t(sm_count()) * 16));
       k_pass_bits<<<grid, 256, 0, s>>>(v, row_offset, n_rows, pass, pass_words, filter->universe_size);
+      k_pass_tile_sums<<<n_wtiles, kWordTile, 0, s>>>(pass, pass_words, tiles, count);
     }
-    k_pass_tile_sums<<<n_wtiles, kWordTile, 0, s>>>(pass, pass_words, tiles, count);
     CR_CUDA(cudaGetLastError());
     tr.mark("pass_bits", s);
     // Pre-filter below half density: compact the passing rows' indices (and
     // norms) and copy those rows into a dense block searched with TMA tiles.
-    uint32_t* idx = comp_scr.as<uint32_t>();
-    float* comp_norms = l2 ? reinterpret_cast<float*>(
-        (reinterpret_cast<uintptr_t>(idx + cap_rows) + 255) & ~uintptr_t(255)) : nullptr;
-    uint16_t* comp = reinterpret_cast<uint16_t*>(
-        (reinterpret_cast<uintptr_t>(l2 ? static_cast<void*>(comp_norms + cap_rows)
-                                        : static_cast<void*>(idx + cap_rows)) + 255) & ~uintptr_t(255));
+    uint32_t* idx = arena.take<uint32_t>(cap_rows * 4);
+    float* comp_norms = l2 ? arena.take<float>(cap_rows * 4) : nullptr;
+    uint16_t* comp = arena.take<uint16_t>(cap_rows * DIM * 2);
     {
       ProfileScope prof_c(CR_KERNEL_TOPK_COMPACT, s);
       k_pass_compact<<<n_wtiles, kCompactThreads, 0, s>>>(pass, pass_words, tiles, n_wtiles, idx, d_total,
                                                     l2 ? norms : nullptr, comp_norms,
                                                     reinterpret_cast<const uint4*>(d_db),
-                                                    reinterpret_cast<uint4*>(comp), uint32_t(cap_rows));
+                                                    reinterpret_cast<uint4*>(comp), uint32_t(cap_rows), count,
+                                                    pa, plan);
       CR_CUDA(cudaGetLastError());
     }
-    k_plan<<<1, 32, 0, s>>>(count, uint32_t(n_rows), slices, slices * EPI_PARTS, k, spec_capable, spec_override,
-                            tiles_override, plan);
     tr.mark("compact_gather", s);
     in.pass = pass;
     in.comp = comp;
