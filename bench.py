@@ -8,7 +8,7 @@ carries 1-8 tags drawn Zipf(s=1.0) over 1,000 tags; the filter is the
 Roaring bitmap of rows carrying any tag of a greedily chosen tag set that
 targets a 10% pass rate. One step = one batch of 1,000 queries: per rank
 cr_filtered_topk over its row range (global row IDs), then (N > 1) an NCCL
-all_gather of the per-rank [1000 x k] lists and cr_topk_merge on rank 0.
+gather (to rank 0) of the per-rank packed [1000 x k] blocks and cr_topk_merge_packed there.
 
 `python bench.py --gpus N --steps K --warmup W [--impl reference]`
 prints ONE JSON line on rank 0.
@@ -478,15 +478,17 @@ def main():
     stream = torch.cuda.current_stream()
 
     # Each shard's top-k lands in one packed block (distances then ids), so one
-    # NCCL all-gather carries it; rank 0 merges the gathered blocks in place.
+    # NCCL gather carries it; rank 0 merges the gathered blocks in place.
     block, block_d, block_i = cr.topk_packed_buffer(N_QUERIES, K, dev)
     gathered = torch.empty((world, block.numel()), dtype=torch.uint8, device=dev)
+    gather_views = list(gathered.unbind(0))
 
     def step(qdev):
         d, i = cr.filtered_topk(db, qdev, K, metric=cr.METRIC_IP, filter=filt, row_offset=lo, stream=stream,
                                 out_dist=block_d, out_ids=block_i)
         if world > 1:
-            dist.all_gather_into_tensor(gathered, block)
+            # Only rank 0 merges: gather the blocks there (NCCL send/recv).
+            dist.gather(block, gather_list=gather_views if rank == 0 else None, dst=0)
             if rank == 0:
                 d, i = cr.topk_merge_packed(gathered, N_QUERIES, K, metric=cr.METRIC_IP, stream=stream)
         return d, i
@@ -586,7 +588,7 @@ def main():
                        "queries_per_step": N_QUERIES, "k": K, "metric": "IP",
                        "pass_rate_target": PASS_TARGET, "pass_rate": pass_rate,
                        "parallelism": f"row-range shards over {world} GPU(s)" +
-                       (", NCCL all_gather of [1000 x k] + merge" if world > 1 else ""),
+                       (", NCCL gather of the packed [1000 x k] blocks to rank 0 + merge" if world > 1 else ""),
                        "l2": "inputs larger than L2 (2.56 GB database streamed every step)"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": None,
