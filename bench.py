@@ -30,6 +30,9 @@ for _p in (REPO / "cu-roaring-bitmap_b200", REPO / "oracle"):
     sys.path.insert(0, str(_p))
 
 N_ROWS = 10_000_000
+# DRAM bytes per searched row of the main k_topk launch, from one ncu capture
+# (dram__bytes_read.sum + dram__bytes_write.sum over 507,149 rows).
+TOPK_DRAM_BYTES_PER_ROW = (133_064_448 + 6_056_192) / 507_149
 DIM = 128
 N_QUERIES = 1000
 K = 100
@@ -591,7 +594,9 @@ def main():
                        (", NCCL gather of the packed [1000 x k] blocks to rank 0 + merge" if world > 1 else ""),
                        "l2": "inputs larger than L2 (2.56 GB database streamed every step)"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                         "frac": achieved / peak, "traffic": None,
+                         "frac": achieved / peak, "traffic": TOPK_DRAM_BYTES_PER_ROW * rows_searched,
+                         "traffic_source": "ncu dram__bytes_read+write of the main k_topk launch on a 5M-row case "
+                                           "(profiles/k_topk_c5_filtered_topk.md), bytes per searched row x rows",
                          "kernel": "k_topk", "kernel_ms": kern_ms,
                          "other_kernels_ms": {"k_merge": float(np.mean(merge_ms)) if merge_ms else None,
                                               "k_pass_compact": float(np.mean(gather_ms)) if gather_ms else None},
