@@ -712,8 +712,8 @@ __global__ void __launch_bounds__(128) k_spec(const uint32_t* pub_top, uint32_t 
 }
 
 // ------------------------------------------------------------------ merge
-constexpr uint32_t MERGE_N = 4096;
-constexpr uint32_t MERGE_THREADS = 512;
+constexpr uint32_t MERGE_N = 2048;
+constexpr uint32_t MERGE_THREADS = 256;
 constexpr uint32_t kMaxListsMerge = 1023;  // partial lists per query in append mode
 
 __device__ __forceinline__ bool better64(float as, int64_t ai, float bs, int64_t bi)
@@ -744,7 +744,7 @@ __device__ void bitonic_sort(float* s, int64_t* id, uint32_t n = MERGE_N)
 
 // One CTA per query: the best k of `parts` sorted lists. kind 0: inputs are
 // internal scores of k_topk; kind 1: inputs are final distances.
-__global__ void __launch_bounds__(MERGE_THREADS, 3) k_merge(const float* part_s, const int64_t* part_id,
+__global__ void __launch_bounds__(MERGE_THREADS, 6) k_merge(const float* part_s, const int64_t* part_id,
                                                          uint32_t parts, uint32_t n_queries,
                                                          uint32_t k, int metric, int kind,
                                                          const __half* queries, uint32_t dim,
