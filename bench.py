@@ -279,6 +279,50 @@ def c2_upload_ids(torch, g, dev):
     ids = ids[torch.randperm(ids.numel(), device=dev, generator=g)]
     return ids.to(torch.int32)
 
+def topk_sweep(torch, cr, db, queries, tags, pk):
+    """The other config-5 cases on the same 10M x 128 database: pass-rate
+    targets 0.1/1/10/50% x k in {10, 100} (IP), and L2 at 10% / k=100.
+    Device-resident timing (CUDA events, 2 warm-up + 5 timed batches each)."""
+    out = []
+    norms = cr.row_norms(db)
+    stream = torch.cuda.current_stream()
+    cases = [(t, kk, cr.METRIC_IP) for t in (0.001, 0.01, 0.10, 0.50) for kk in (10, 100)]
+    cases.append((0.10, 100, cr.METRIC_L2))
+    filters = {}
+    for target, kk, metric in cases:
+        if target not in filters:
+            tset = choose_tag_set(torch, db.device, target)
+            m = torch.isin(tags, tset).any(dim=1)
+            ids = torch.nonzero(m).flatten().to(torch.int32)
+            filters[target] = (cr.upload_from_ids(ids, db.shape[0], bitmap_threshold=cr.PROMOTE_AUTO), ids.numel())
+        filt, n_pass = filters[target]
+        kw = dict(metric=metric, filter=filt, stream=stream, db_norms=norms if metric == cr.METRIC_L2 else None)
+        for _ in range(2):
+            cr.filtered_topk(db, queries, kk, **kw)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        cr.profile_enable(False)
+        cr.profile_enable(True)
+        e0.record(stream)
+        for _ in range(5):
+            cr.filtered_topk(db, queries, kk, **kw)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        kern, _ = cr.profile_mean_ms(cr.KERNEL_TOPK)
+        cr.profile_enable(False)
+        ms = e0.elapsed_time(e1) / 5
+        rows = n_pass if 2 * n_pass <= db.shape[0] else db.shape[0]
+        tflops = 2.0 * N_QUERIES * rows * DIM / (kern / 1e3) / 1e12 if kern else None
+        out.append({"pass_target": target, "pass_rate": n_pass / db.shape[0], "k": kk,
+                    "metric": "L2" if metric == cr.METRIC_L2 else "IP", "qps": N_QUERIES / (ms / 1e3),
+                    "ms_per_batch": ms, "k_topk_ms": kern, "rows_searched": rows,
+                    "k_topk_tflops": tflops,
+                    "roofline_frac": (tflops / pk["bf16_tflops_sustained"]) if tflops else None})
+    for f, _ in filters.values():
+        f.free()
+    return out
+
+
 def secondary_metrics(torch, cr, pk):
     """Rank 0, N=1: contains Gq/s (config 4 shape), AND set-op GB/s,
     upload (config 2) and multi_and / to_csr (config 3)."""
@@ -469,7 +513,8 @@ def main():
     lo, hi = cr.shard_range(n_rows, rank, world)
     db = gen_rows(torch, lo, hi, dev)
     tset = choose_tag_set(torch, dev, PASS_TARGET)
-    mask = torch.isin(gen_tags(torch, lo, hi, dev), tset).any(dim=1)
+    tags_local = gen_tags(torch, lo, hi, dev)
+    mask = torch.isin(tags_local, tset).any(dim=1)
     pass_ids = (torch.nonzero(mask).flatten() + lo).to(torch.int32)
     n_pass = torch.tensor([pass_ids.numel()], device=dev, dtype=torch.int64)
     if world > 1:
@@ -568,9 +613,11 @@ def main():
             cpu = {"value": qps, "unit": "queries/s", "cores": os.cpu_count() or 1, "kind": "port",
                    "sample": desc, "seconds": dt}
         if not args.no_secondary and world == 1:
+            sweep = topk_sweep(torch, cr, db, queries, tags_local, pk)
             del db
             torch.cuda.empty_cache()
             secondary = secondary_metrics(torch, cr, pk)
+            secondary["topk_sweep"] = sweep
 
     if rank == 0:
         rows_local = hi - lo

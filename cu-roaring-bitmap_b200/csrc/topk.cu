@@ -662,7 +662,11 @@ __device__ void make_plan(const uint32_t* count, const PlanArgs a, SearchPlan* p
   if (spec_capable && pl.n_rows > 0 && 3 * n_lists <= 256) {
     const double sample = double(min(uint64_t(pl.n_rows), uint64_t(slices) * min(pl.tps, pl.spec_tiles) * BN));
     const double f = sample / double(pl.n_rows);
-    if (f <= 0.5) {
+    if (f > 0.5) {
+      // Most rows are in the sample: use the union's k-th best, which needs
+      // no luck (k distinct rows are at or above it) and is nearly exact.
+      if (k <= 3 * n_lists) pl.spec_j = k;
+    } else {
       const double lam = double(k) * f;
       // Smallest j >= 1 with P(X >= j) = 1 - P(X < j) below 1e-9, X ~ Poisson(lam).
       double term = exp(-lam), below = 0.0;  // P(X = j), P(X < j)
@@ -672,7 +676,7 @@ __device__ void make_plan(const uint32_t* count, const PlanArgs a, SearchPlan* p
         below += term;
         term *= lam / double(j + 1);
       }
-      if (j <= 3 * n_lists) pl.spec_j = j;
+      if (j <= 3 * n_lists) pl.spec_j = min(j, k);  // rank k never needs luck
     }
     if (spec_override >= 0) pl.spec_j = min(uint32_t(spec_override), 3 * n_lists);
   }
@@ -844,19 +848,23 @@ __global__ void __launch_bounds__(MERGE_THREADS, 6) k_merge(const float* part_s,
     if (!l2) return x;
     return kind != 1 ? s_qn - x : -x;
   };
-  auto select_out = [&](uint32_t n) -> bool {
-    // Radix select (8-bit digits, most significant first) of the k-th best
-    // score key T; the selected set is every survivor with key >= T.
+  // Best k of a set of entries, written to the outputs: radix select of the
+  // k-th best score key T (8-bit digits, most significant first), then an
+  // exact rank (score desc, id asc) of the entries at or above T. `each(fn)`
+  // calls fn(score, id_of) for every entry (all threads, strided); `known_n`
+  // is the entry count when known (UINT32_MAX otherwise). False (nothing
+  // written) when more than kSelMax entries tie at or above T.
+  auto select_k = [&](auto&& each, uint32_t known_n) -> bool {
     uint32_t thr = 0;
-    if (n > k) {
+    if (known_n > k) {
       uint32_t prefix = 0, mask = 0, rem = k;
       for (int shift = 24; shift >= 0; shift -= 8) {
         for (uint32_t b = threadIdx.x; b < 256; b += MERGE_THREADS) s_hist[b] = 0;
         __syncthreads();
-        for (uint32_t e = threadIdx.x; e < n; e += MERGE_THREADS) {
-          const uint32_t key = score_key(s[e]);
+        each([&](float x, auto) {
+          const uint32_t key = score_key(x);
           if ((key & mask) == prefix) atomicAdd(&s_hist[(key >> shift) & 255u], 1u);
-        }
+        });
         __syncthreads();
         if (threadIdx.x < 32) {
           const uint32_t lane = threadIdx.x;
@@ -869,8 +877,12 @@ __global__ void __launch_bounds__(MERGE_THREADS, 6) k_merge(const float* part_s,
             const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, x, o);
             if (lane >= o) x += y;
           }
-          const uint32_t before = x - tot;  // survivors in higher digits
-          if (before < rem && rem <= x) {
+          // Everything still matching the prefix is selected when it is no
+          // more than the rank still wanted.
+          const uint32_t matching = __shfl_sync(0xFFFFFFFFu, x, 31);
+          if (lane == 0) s_sel[2] = matching <= rem ? 1u : 0u;
+          const uint32_t before = x - tot;  // entries in higher digits
+          if (matching > rem && before < rem && rem <= x) {
             uint32_t acc = before;
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
@@ -884,26 +896,27 @@ __global__ void __launch_bounds__(MERGE_THREADS, 6) k_merge(const float* part_s,
           }
         }
         __syncthreads();
+        if (s_sel[2]) break;  // thr = prefix: every entry at or above it
         prefix = s_sel[0];
         rem = s_sel[1];
         mask |= 255u << shift;
       }
       thr = prefix;
-      if (threadIdx.x == 0 && thr < spec) atomicOr(err, kErrSpec);
-    } else if (threadIdx.x == 0 && spec && !s_over) {
-      atomicOr(err, kErrSpec);  // fewer than k kept: the bound may have dropped some
     }
+    // A speculative bound must not be above the k-th best kept (fewer than k
+    // kept counts as above): conservative when the select stopped early.
+    if (threadIdx.x == 0 && spec && !s_over && thr < spec) atomicOr(err, kErrSpec);
     // Compact key >= T into the tail slots.
     if (threadIdx.x == 0) s_m = 0;
     __syncthreads();
     float* cs = s + (MERGE_N - kSelMax);
     int64_t* cid = id + (MERGE_N - kSelMax);
-    for (uint32_t e = threadIdx.x; e < n; e += MERGE_THREADS) {
-      if (score_key(s[e]) >= thr) {
+    each([&](float x, auto id_of) {
+      if (score_key(x) >= thr) {
         const uint32_t slot = atomicAdd(&s_m, 1u);
-        if (slot < kSelMax) { cs[slot] = s[e]; cid[slot] = id[e]; }
+        if (slot < kSelMax) { cs[slot] = x; cid[slot] = id_of(); }
       }
-    }
+    });
     __syncthreads();
     const uint32_t m = s_m;
     if (m <= kSelMax) {
@@ -926,6 +939,14 @@ __global__ void __launch_bounds__(MERGE_THREADS, 6) k_merge(const float* part_s,
       return true;
     }
     return false;
+  };
+  // The entries in s/id [0, n) (n <= MERGE_N - kSelMax).
+  auto select_out = [&](uint32_t n) -> bool {
+    return select_k(
+        [&](auto&& fn) {
+          for (uint32_t e = threadIdx.x; e < n; e += MERGE_THREADS) fn(s[e], [&] { return id[e]; });
+        },
+        n);
   };
   if (kind == 2) {
     // Per-list counts -> prefix in shared memory (flattened candidate index
@@ -979,6 +1000,24 @@ __global__ void __launch_bounds__(MERGE_THREADS, 6) k_merge(const float* part_s,
     const uint32_t n = s_fill;
     __syncthreads();  // every thread has n before the fallback below resets s_fill
     if (n <= MERGE_N - kSelMax && select_out(n)) return;
+    if (n > MERGE_N - kSelMax) {
+      // More survivors than shared memory holds: select straight from the
+      // candidate arrays (one warp per list, lanes over its entries).
+      const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+      auto each_candidate = [&](auto&& fn) {
+        for (uint32_t l = warp; l < nl; l += MERGE_THREADS / 32) {
+          const uint32_t cnt = min(s_pre[l + 1] - s_pre[l], cap);
+          const size_t base = (size_t(q) * n_lists + l) * cap;
+          for (uint32_t e = lane; e < cnt; e += 32) {
+            const float x = part_s[base + e];
+            const uint32_t r = cand_r[base + e];
+            if (x >= bound && r < n_rows)
+              fn(x, [&] { return int64_t(row_map ? __ldg(row_map + r) : r) + int64_t(row_offset); });
+          }
+        }
+      };
+      if (select_k(each_candidate, 0xFFFFFFFFu)) return;
+    }
     if (n <= MERGE_N) {
       // Too many ties at the k-th score for the rank pass: sort the
       // survivors (already in [0, n)).
