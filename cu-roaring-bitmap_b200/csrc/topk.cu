@@ -522,13 +522,22 @@ __global__ void __launch_bounds__(THREADS, 1)
           else { top3 = x; }
         }
       };
-      const bool whole = APPEND && !l2 && !pass && row0 + BN <= n_rows && p.debug == 0;
+      // Whole-part fast path: every row of the part is searched (no mask, or
+      // both of its mask words full).
+      const bool whole = APPEND && row0 + BN <= n_rows && p.debug == 0 &&
+                         (!pass || (__ldg(pass + ((row0 >> 5) + chalf * 2)) & __ldg(pass + ((row0 >> 5) + chalf * 2 + 1))) ==
+                                       0xFFFFFFFFu);
       if (whole) {
         // Every row of this part passes: one 64-column TMEM load and one
         // 6-level max tree for the part's two chunks.
         static_assert(PART_CHUNKS == 2, "64-column part");
         float v[64];
         tmem_ld64(tmem + ((quarter * 32u) << 16) + a * BN + chalf * 64, v);
+        if (l2) {  // internal score 2 q.x - |x|^2 (same row norms for every lane: broadcast loads)
+          const float* nr = norms + row0 + chalf * 64;
+#pragma unroll
+          for (int j = 0; j < 64; ++j) v[j] = 2.f * v[j] - __ldg(nr + j);
+        }
         // Max trees of the two 32-row halves (the slow path then runs only
         // for a half that has a candidate in some lane).
         float t[32];
@@ -634,7 +643,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 }
 
 // The search plan from the pass count (`count`, null = every
-// shard row passes). Below half density the passing rows are compacted and
+// shard row passes). Up to 3/4 of the rows passing, the passing rows are compacted and
 // searched; otherwise the shard is searched with the pass bitset. Then the
 // tiling over `slices`, and the speculative bound's rank: the prologue sees
 // about `sample` of the searched rows, and the spec_j-th best of the union
@@ -644,6 +653,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 // and tests) forces the rank when >= 0; tiles_override the prologue length.
 struct PlanArgs {
   uint32_t shard_rows, slices, n_lists, k, spec_capable;
+  uint32_t cap_rows;  // the compacted copy holds up to this many rows
   int spec_override, tiles_override;
 };
 __device__ void make_plan(const uint32_t* count, const PlanArgs a, SearchPlan* plan)
@@ -653,7 +663,7 @@ __device__ void make_plan(const uint32_t* count, const PlanArgs a, SearchPlan* p
   const int spec_override = a.spec_override, tiles_override = a.tiles_override;
   SearchPlan pl{};
   const uint32_t n_pass = count ? *count : shard_rows;
-  pl.dense = (count == nullptr || uint64_t(n_pass) * 2 > shard_rows) ? 1u : 0u;
+  pl.dense = (count == nullptr || n_pass > a.cap_rows) ? 1u : 0u;
   pl.n_rows = pl.dense ? shard_rows : n_pass;
   pl.n_tiles = (pl.n_rows + BN - 1) / BN;
   pl.tps = max(1u, (pl.n_tiles + slices - 1) / slices);
@@ -843,6 +853,7 @@ __global__ void __launch_bounds__(MERGE_THREADS, 6) k_merge(const float* part_s,
   __shared__ uint32_t s_hist[256];
   __shared__ uint32_t s_sel[3];
   __shared__ uint32_t s_m;
+  __shared__ uint32_t s_ge_spec;
   auto dist_of = [&](float x, int64_t r) {
     if (r < 0) return l2 ? INFINITY : -INFINITY;
     if (!l2) return x;
@@ -903,21 +914,21 @@ __global__ void __launch_bounds__(MERGE_THREADS, 6) k_merge(const float* part_s,
       }
       thr = prefix;
     }
-    // A speculative bound must not be above the k-th best kept (fewer than k
-    // kept counts as above): conservative when the select stopped early.
-    if (threadIdx.x == 0 && spec && !s_over && thr < spec) atomicOr(err, kErrSpec);
-    // Compact key >= T into the tail slots.
-    if (threadIdx.x == 0) s_m = 0;
+    // Compact key >= T into the tail slots; count the entries at or above a
+    // speculative bound (it was safe iff at least k are).
+    if (threadIdx.x == 0) { s_m = 0; s_ge_spec = 0; }
     __syncthreads();
     float* cs = s + (MERGE_N - kSelMax);
     int64_t* cid = id + (MERGE_N - kSelMax);
     each([&](float x, auto id_of) {
+      if (spec && score_key(x) >= spec) atomicAdd(&s_ge_spec, 1u);
       if (score_key(x) >= thr) {
         const uint32_t slot = atomicAdd(&s_m, 1u);
         if (slot < kSelMax) { cs[slot] = x; cid[slot] = id_of(); }
       }
     });
     __syncthreads();
+    if (threadIdx.x == 0 && spec && !s_over && s_ge_spec < k) atomicOr(err, kErrSpec);
     const uint32_t m = s_m;
     if (m <= kSelMax) {
       // Exact rank of each selected entry (score desc, id asc); the best k
@@ -1712,9 +1723,12 @@ extern "C" int cr_filtered_topk(const uint16_t* d_db, const float* d_db_norms, u
   // the end of the call.
   const uint64_t pass_words = (n_rows + 31) / 32;
   const uint32_t n_wtiles = div_up(pass_words, kWordTile);
-  const uint64_t cap_rows = filter ? std::max<uint64_t>(1, n_rows / 2) : 0;
+  // Up to 3/4 of the rows passing, copying the passing rows (512 B of HBM
+  // traffic each) is cheaper than searching every row with the mask.
+  const uint64_t cap_rows = filter ? std::max<uint64_t>(1, n_rows * 3 / 4) : 0;
   Scratch kidx_holder;
-  const PlanArgs pa{uint32_t(n_rows), slices, slices * EPI_PARTS, k, spec_capable, spec_override, tiles_override};
+  const PlanArgs pa{uint32_t(n_rows), slices, slices * EPI_PARTS, k, spec_capable, uint32_t(cap_rows),
+                    spec_override, tiles_override};
   if (!filter) {
     k_plan<<<1, 32, 0, s>>>(nullptr, pa, plan);
   } else {
@@ -1735,7 +1749,7 @@ extern "C" int cr_filtered_topk(const uint16_t* d_db, const float* d_db_norms, u
     }
     CR_CUDA(cudaGetLastError());
     tr.mark("pass_bits", s);
-    // Pre-filter below half density: compact the passing rows' indices (and
+    // Pre-filter up to 3/4 density: compact the passing rows' indices (and
     // norms) and copy those rows into a dense block searched with TMA tiles.
     uint32_t* idx = arena.take<uint32_t>(cap_rows * 4);
     float* comp_norms = l2 ? arena.take<float>(cap_rows * 4) : nullptr;

@@ -141,7 +141,7 @@ def test_topk_all_ties_falls_back_exactly(cr, torch_):
         assert (i.cpu().numpy() == np.arange(k)[None, :]).all()
 
 
-@pytest.mark.parametrize("kind", ["runs", "negated", "array_sparse", "offset_not_32"])
+@pytest.mark.parametrize("kind", ["runs", "runs_dense", "negated", "array_sparse", "offset_not_32"])
 def test_topk_filter_container_kinds(cr, oracle, torch_, kind):
     """Filters made of RUN containers, a negated (complement-stored) filter,
     sparse ARRAY containers, and a shard offset that is not a multiple of 32
@@ -151,14 +151,16 @@ def test_topk_filter_container_kinds(cr, oracle, torch_, kind):
     rng = np.random.default_rng(8)
     if kind == "runs":
         ids = np.concatenate([np.arange(s, s + 3000) for s in range(0, n - 3000, 9000)]).astype(np.uint32)
+    elif kind == "runs_dense":  # ~80% pass in long runs: searched densely, mostly full mask words
+        ids = np.concatenate([np.arange(s, min(n, s + 8000)) for s in range(0, n, 10000)]).astype(np.uint32)
     elif kind == "negated":
         ids = np.flatnonzero(rng.random(n) < 0.9).astype(np.uint32)
     else:
         ids = np.flatnonzero(rng.random(n) < 0.003).astype(np.uint32)
     lo = 0 if kind != "offset_not_32" else 1000 + 7
     filt = cr.upload_from_ids(ids, n, bitmap_threshold=4096)
-    if kind == "runs":
-        assert filt.raw.n_run_containers > 0
+    if kind in ("runs", "runs_dense"):
+        assert filt.raw.n_run_containers > 0 or filt.raw.negated
     if kind == "negated":
         assert filt.raw.negated
     words = np.zeros((n + 31) // 32, dtype=np.uint32)
