@@ -13,3 +13,4 @@
 #include "cu_roaring/device/roaring_view.cuh"
 #include "cu_roaring/device/roaring_warp_query.cuh"
 #include "cu_roaring/device/make_view.cuh"
+#include "cu_roaring/filters/roaring_filter.cuh"

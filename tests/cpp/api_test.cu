@@ -4,7 +4,8 @@
 // warp_contains inside user kernels), compiled against this engine's headers
 // and linked to libcuroaring_b200.so. Cases follow the reference's
 // test/test_promote.cu, test/test_complement.cu, test/test_device_query.cu and
-// test/test_decompress.cu. Prints one line per check and exits non-zero on
+// test/test_decompress.cu, plus a graph-traversal harness for the
+// roaring_filter adapter. Prints one line per check and exits non-zero on
 // any failure.
 #include <algorithm>
 #include <cstdio>
@@ -33,6 +34,79 @@ __global__ void user_warp_contains(cu_roaring::GpuRoaringView v, const uint32_t*
   const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
   const bool hit = cu_roaring::warp_contains(v, i < n ? q[i] : 0u);  // all lanes call it
   if (i < n) out[i] = hit;
+}
+
+// Graph-traversal harness for cu_roaring::filtering::roaring_filter: a
+// deterministic walk over a fixed-degree graph, one warp per query. At every
+// hop the warp scores the current node's 32 neighbours, records the best one
+// the filter passes (or 0xFFFFFFFF) and moves to the best neighbour overall
+// (traversal ignores the filter, as graph search does).
+__host__ __device__ inline uint32_t mix32(uint32_t x)
+{
+  x ^= x >> 16; x *= 0x7feb352du; x ^= x >> 15; x *= 0x846ca68bu; x ^= x >> 16;
+  return x;
+}
+__host__ __device__ inline uint32_t walk_start(uint32_t q, uint32_t n) { return mix32(q * 2654435761u + 1u) % n; }
+__host__ __device__ inline uint32_t walk_score(uint32_t q, uint32_t nb) { return mix32(nb ^ (q * 0x9e3779b9u)) | 1u; }
+
+__global__ void graph_walk(cu_roaring::filtering::roaring_filter f, const uint32_t* adj, uint32_t n_nodes,
+                           uint32_t n_queries, uint32_t hops, uint32_t* out, int warp_form)
+{
+  const uint32_t q = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (q >= n_queries) return;  // whole warps
+  uint32_t cur = walk_start(q, n_nodes);
+  for (uint32_t h = 0; h < hops; ++h) {
+    const uint32_t nb = adj[size_t(cur) * 32 + lane];
+    const uint32_t sc = walk_score(q, nb);
+    const bool pass = warp_form ? f.warp_test(nb) : f(q, nb);
+    const uint32_t m_all = __reduce_max_sync(0xFFFFFFFFu, sc);
+    const uint32_t next = __reduce_min_sync(0xFFFFFFFFu, sc == m_all ? nb : 0xFFFFFFFFu);
+    const uint32_t m_pass = __reduce_max_sync(0xFFFFFFFFu, pass ? sc : 0u);
+    const uint32_t best = m_pass ? __reduce_min_sync(0xFFFFFFFFu, (pass && sc == m_pass) ? nb : 0xFFFFFFFFu)
+                                 : 0xFFFFFFFFu;
+    if (lane == 0) out[size_t(q) * hops + h] = best;
+    cur = next;
+  }
+}
+
+static void check_graph_walk(const cu_roaring::GpuRoaring& bm, const std::vector<bool>& truth, uint32_t offset,
+                             const char* what)
+{
+  const uint32_t n_nodes = 1u << 20, n_queries = 2048, hops = 24;
+  std::vector<uint32_t> adj(size_t(n_nodes) * 32);
+  std::mt19937 gen(7);
+  for (auto& a : adj) a = gen() % n_nodes;
+  // Host replay with plain membership.
+  std::vector<uint32_t> want(size_t(n_queries) * hops);
+  for (uint32_t q = 0; q < n_queries; ++q) {
+    uint32_t cur = walk_start(q, n_nodes);
+    for (uint32_t h = 0; h < hops; ++h) {
+      uint32_t m_all = 0, next = 0xFFFFFFFFu, m_pass = 0, best = 0xFFFFFFFFu;
+      for (uint32_t j = 0; j < 32; ++j) {
+        const uint32_t nb = adj[size_t(cur) * 32 + j], sc = walk_score(q, nb);
+        if (sc > m_all || (sc == m_all && nb < next)) { m_all = sc; next = nb; }
+        if (truth[nb + offset] && (sc > m_pass || (sc == m_pass && nb < best))) { m_pass = sc; best = nb; }
+      }
+      want[size_t(q) * hops + h] = best;
+      cur = next;
+    }
+  }
+  uint32_t *d_adj = nullptr, *d_out = nullptr;
+  cudaMalloc(&d_adj, adj.size() * 4);
+  cudaMalloc(&d_out, want.size() * 4);
+  cudaMemcpy(d_adj, adj.data(), adj.size() * 4, cudaMemcpyHostToDevice);
+  const cu_roaring::filtering::roaring_filter f(bm, offset);  // one line, no make_view
+  for (int warp_form = 0; warp_form < 2; ++warp_form) {
+    cudaMemset(d_out, 0, want.size() * 4);
+    graph_walk<<<n_queries * 32 / 256, 256>>>(f, d_adj, n_nodes, n_queries, hops, d_out, warp_form);
+    std::vector<uint32_t> got(want.size());
+    cudaMemcpy(got.data(), d_out, got.size() * 4, cudaMemcpyDeviceToHost);
+    char msg[160];
+    std::snprintf(msg, sizeof msg, "%s (%s form)", what, warp_form ? "warp" : "per-thread");
+    EXPECT(got == want, msg);
+  }
+  cudaFree(d_adj);
+  cudaFree(d_out);
 }
 
 static std::vector<uint8_t> query(const cu_roaring::GpuRoaring& bm, const std::vector<uint32_t>& q,
@@ -172,6 +246,33 @@ int main()
     check_against(r, t, q, "multi_and with negation");
     gpu_roaring_free(r);
     for (auto& x : in) gpu_roaring_free(x);
+  }
+  {  // roaring_filter in a graph walk: mixed containers, shard offset, negation
+    const uint32_t offset = 3 * 65536 + 5, U = (1u << 20) + offset + 1000;
+    std::vector<uint32_t> ids;
+    std::vector<bool> t(U, false);
+    std::mt19937 gen(11);
+    for (uint32_t i = 0; i < U; ++i) {
+      const uint32_t chunk = i >> 16;
+      bool in = false;
+      if (chunk % 3 == 0) in = gen() % 100 == 0;            // sparse: ARRAY
+      else if (chunk % 3 == 1) in = gen() % 2 == 0;         // dense: BITMAP
+      else in = (i / 2000) % 2 == 0;                        // long runs: RUN
+      if (in) { ids.push_back(i); t[i] = true; }
+    }
+    auto bm = upload_from_ids(ids.data(), ids.size(), U);
+    EXPECT(bm.n_array_containers > 0 && bm.n_bitmap_containers > 0 && bm.n_run_containers > 0,
+           "roaring_filter: mixed container types");
+    check_graph_walk(bm, t, offset, "roaring_filter graph walk, offset shard");
+    gpu_roaring_free(bm);
+    std::vector<uint32_t> dense;
+    std::vector<bool> td(U, false);
+    for (uint32_t i = 0; i < U; ++i)
+      if (gen() % 10 != 0) { dense.push_back(i); td[i] = true; }
+    auto neg = upload_from_ids(dense.data(), dense.size(), U);
+    EXPECT(neg.negated, "roaring_filter: complement-stored filter");
+    check_graph_walk(neg, td, 0, "roaring_filter graph walk, negated");
+    gpu_roaring_free(neg);
   }
   {  // error convention: an ID outside the universe throws std::runtime_error
     std::vector<uint32_t> ids = {5, 500};
