@@ -85,6 +85,11 @@ void build_key_index(const uint16_t* keys, uint32_t n, uint16_t* kidx, uint32_t 
                      cudaStream_t s);
 
 int sm_count();
+
+// Roaring image of a flat device bitset (upload.cu): canonical container
+// types under `thr`, complement above half density, bits >= U ignored.
+void upload_device_bitset(const uint32_t* d_words, uint64_t n_words, uint32_t U, uint32_t thr,
+                          cudaStream_t s, cr_gpu_roaring* out);
 uint64_t l2_bytes(int device);
 uint32_t resolve_auto(uint32_t U, int device);
 

@@ -35,7 +35,7 @@ EXPORTED_SYMBOLS = (
     "cr_promote_auto", "cr_deep_copy", "cr_set_operation", "cr_multi_and", "cr_multi_or",
     "cr_decompress_to_bitset", "cr_decompress_to_bitset_alloc", "cr_enumerate_ids_i64",
     "cr_enumerate_ids_u32", "cr_enumerate_ids_alloc", "cr_enumerate_ids_u32_noalloc", "cr_contains_batch", "cr_filtered_topk",
-    "cr_row_norms", "cr_topk_merge", "cr_topk_merge_packed", "cr_filtered_topk_check", "cr_profile_enable", "cr_profile_last_ms", "cr_profile_sum_ms",
+    "cr_row_norms", "cr_topk_merge", "cr_topk_merge_packed", "cr_upload_portable", "cr_filtered_topk_check", "cr_profile_enable", "cr_profile_last_ms", "cr_profile_sum_ms",
 )
 
 
@@ -87,6 +87,7 @@ _sigs = {
     "cr_profile_last_ms": ([_i32, C.POINTER(C.c_float)], _i32),
     "cr_topk_merge_packed": ([C.c_void_p, C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, _i32, C.c_void_p,
                               C.c_void_p, C.c_void_p], _i32),
+    "cr_upload_portable": ([C.c_void_p, C.c_uint64, C.c_uint32, C.c_void_p, C.c_uint32, C.c_void_p], _i32),
     "cr_filtered_topk_check": ([], _i32),
     "cr_profile_sum_ms": ([_i32, C.POINTER(C.c_float), C.POINTER(C.c_uint32)], _i32),
 }
@@ -238,6 +239,15 @@ def upload_from_device_bitset(words, universe_size: int, stream=None,
     _check(_lib.cr_upload_from_device_bitset(_dev_ptr(words) if words.numel() else None, words.numel(),
                                              universe_size, _stream_ptr(stream), bitmap_threshold,
                                              C.byref(out.raw)), "upload_from_device_bitset")
+    return out
+
+
+def upload_portable(data: bytes, universe_size: int, stream=None, bitmap_threshold: int = PROMOTE_AUTO) -> GpuRoaring:
+    """A bitmap in the portable Roaring serialization (bytes) -> GpuRoaring."""
+    out = GpuRoaring()
+    buf = C.create_string_buffer(bytes(data), len(data)) if len(data) else None
+    _check(_lib.cr_upload_portable(C.cast(buf, C.c_void_p) if buf is not None else None, len(data), universe_size,
+                                   _stream_ptr(stream), bitmap_threshold, C.byref(out.raw)), "upload_portable")
     return out
 
 

@@ -19,6 +19,19 @@ inline void gpu_roaring_free_async(GpuRoaring& bitmap, cudaStream_t stream)
                 "gpu_roaring_free_async");
 }
 
+// A bitmap in the portable Roaring serialization (the format other Roaring
+// libraries write to disk), loaded straight into device memory: the
+// replacement for the CRoaring-typed upload() path. No reference counterpart.
+inline GpuRoaring upload_portable(const void* data, size_t n_bytes, uint32_t universe_size,
+                                  cudaStream_t stream = 0, uint32_t bitmap_threshold = PROMOTE_AUTO)
+{
+  GpuRoaring out{};
+  detail::check(cr_upload_portable(data, n_bytes, universe_size, detail::s(stream), bitmap_threshold,
+                                   detail::c(out)),
+                "upload_portable");
+  return out;
+}
+
 inline GpuRoaringMeta get_meta(const GpuRoaring& b)
 {
   GpuRoaringMeta m{};

@@ -94,6 +94,17 @@ int cr_upload_from_device_ids(const uint32_t* d_ids, uint64_t n_ids, uint32_t un
                               cr_stream_t stream, uint32_t bitmap_threshold,
                               cr_gpu_roaring* out);
 
+/* A bitmap in the portable Roaring serialization (the published,
+ * library-independent format: cookie 12346 / 12347, (key, cardinality - 1)
+ * headers, optional offsets, ARRAY / BITMAP / RUN payloads) -> GpuRoaring
+ * with canonical container types under bitmap_threshold and the complement
+ * above half density. Replaces loading through CRoaring and
+ * upload(const roaring_bitmap_t*) (reference src/upload.cpp:89-225, 290-296;
+ * bench/bench_from_disk.cu). Returns CR_ERR_INVALID for a malformed buffer
+ * and CR_ERR_RANGE for members >= universe_size. */
+int cr_upload_portable(const void* data, uint64_t n_bytes, uint32_t universe_size, cr_stream_t stream,
+                       uint32_t bitmap_threshold, cr_gpu_roaring* out);
+
 /* Replace upload_from_bitset / upload_from_device_bitset (reference
  * src/upload_ids.cu:806-893, include/cu_roaring/detail/upload_ids.cuh:48-56).
  * Bit i is (words[i/32] >> (i%32)) & 1. Bits >= universe_size are ignored.

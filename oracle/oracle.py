@@ -189,6 +189,17 @@ def promote_to_bitmap(a: OracleBitmap) -> OracleBitmap:
     return r
 
 
+def serialize_portable(ids, allow_runs: bool = True) -> bytes:
+    """Portable Roaring serialization of a set of uint32 IDs (any order, duplicates ok)."""
+    a = np.unique(np.asarray(ids, dtype=np.uint32))
+    f = lib().or_serialize_portable
+    f.restype = C.c_uint64
+    n = f(a.ctypes.data if a.size else None, C.c_uint64(a.size), int(allow_runs), None, C.c_uint64(0))
+    buf = (C.c_uint8 * max(1, n))()
+    f(a.ctypes.data if a.size else None, C.c_uint64(a.size), int(allow_runs), buf, C.c_uint64(n))
+    return bytes(buf)[:n]
+
+
 def topk(db_f16: np.ndarray, queries_f16: np.ndarray, k: int, metric: int = 0,
          pass_bits: np.ndarray | None = None, threads: int = 0):
     db = np.ascontiguousarray(db_f16).view(np.uint16)

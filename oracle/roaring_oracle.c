@@ -791,3 +791,92 @@ void or_topk_f32(const float* dbf, const float* norms, uint64_t n_rows, uint32_t
   }
   for (int t = 0; t < n_threads; ++t) pthread_join(th[t], NULL);
 }
+
+
+/* ---- portable serialization (published RoaringFormatSpec) ---------------- */
+
+static void put16(uint8_t* p, uint32_t v) { p[0] = (uint8_t)v; p[1] = (uint8_t)(v >> 8); }
+static void put32(uint8_t* p, uint32_t v) { put16(p, v & 0xFFFFu); put16(p + 2, v >> 16); }
+
+uint64_t or_serialize_portable(const uint32_t* ids, uint64_t n, int allow_runs, uint8_t* out, uint64_t cap)
+{
+  /* Containers: [begin, end) ranges of ids with one high half. */
+  uint64_t n_cont = 0;
+  for (uint64_t i = 0; i < n; ++i)
+    if (i == 0 || (ids[i] >> 16) != (ids[i - 1] >> 16)) ++n_cont;
+  uint64_t* begin = (uint64_t*)malloc(sizeof(uint64_t) * (n_cont + 1));
+  uint32_t* runs = (uint32_t*)malloc(sizeof(uint32_t) * (n_cont + 1));
+  uint8_t* kind = (uint8_t*)malloc(n_cont + 1); /* 0 array, 1 bitmap, 2 run */
+  uint64_t c = 0;
+  for (uint64_t i = 0; i < n; ++i)
+    if (i == 0 || (ids[i] >> 16) != (ids[i - 1] >> 16)) begin[c++] = i;
+  begin[n_cont] = n;
+  int any_run = 0;
+  for (c = 0; c < n_cont; ++c) {
+    const uint64_t b = begin[c], e = begin[c + 1], card = e - b;
+    uint32_t r = 0;
+    for (uint64_t i = b; i < e; ++i)
+      if (i == b || ids[i] != ids[i - 1] + 1) ++r;
+    runs[c] = r;
+    const uint64_t plain = card <= 4096 ? 2 * card : 8192;
+    kind[c] = (allow_runs && 2 + 4 * (uint64_t)r < plain) ? 2 : (card <= 4096 ? 0 : 1);
+    if (kind[c] == 2) any_run = 1;
+  }
+  const int offsets = !any_run || n_cont >= 4;
+  uint64_t head = any_run ? 4 + (n_cont + 7) / 8 : 8;
+  head += 4 * n_cont + (offsets ? 4 * n_cont : 0);
+  uint64_t total = head;
+  for (c = 0; c < n_cont; ++c) {
+    const uint64_t card = begin[c + 1] - begin[c];
+    total += kind[c] == 2 ? 2 + 4 * (uint64_t)runs[c] : (kind[c] == 0 ? 2 * card : 8192);
+  }
+  if (out && cap >= total) {
+    memset(out, 0, total);
+    uint64_t pos;
+    if (any_run) {
+      put32(out, 12347u | ((uint32_t)(n_cont - 1) << 16));
+      for (c = 0; c < n_cont; ++c)
+        if (kind[c] == 2) out[4 + c / 8] |= (uint8_t)(1u << (c % 8));
+      pos = 4 + (n_cont + 7) / 8;
+    } else {
+      put32(out, 12346u);
+      put32(out + 4, (uint32_t)n_cont);
+      pos = 8;
+    }
+    for (c = 0; c < n_cont; ++c) {
+      put16(out + pos + 4 * c, ids[begin[c]] >> 16);
+      put16(out + pos + 4 * c + 2, (uint32_t)(begin[c + 1] - begin[c] - 1));
+    }
+    pos += 4 * n_cont;
+    const uint64_t offs = pos;
+    if (offsets) pos += 4 * n_cont;
+    for (c = 0; c < n_cont; ++c) {
+      const uint64_t b = begin[c], e = begin[c + 1];
+      if (offsets) put32(out + offs + 4 * c, (uint32_t)pos);
+      if (kind[c] == 0) {
+        for (uint64_t i = b; i < e; ++i, pos += 2) put16(out + pos, ids[i] & 0xFFFFu);
+      } else if (kind[c] == 1) {
+        for (uint64_t i = b; i < e; ++i) {
+          const uint32_t lo = ids[i] & 0xFFFFu;
+          out[pos + lo / 8] |= (uint8_t)(1u << (lo % 8)); /* little-endian words: bit lo at byte lo/8 */
+        }
+        pos += 8192;
+      } else {
+        put16(out + pos, runs[c]);
+        pos += 2;
+        for (uint64_t i = b; i < e;) {
+          uint64_t j = i;
+          while (j + 1 < e && ids[j + 1] == ids[j] + 1) ++j;
+          put16(out + pos, ids[i] & 0xFFFFu);
+          put16(out + pos + 2, (uint32_t)(j - i));
+          pos += 4;
+          i = j + 1;
+        }
+      }
+    }
+  }
+  free(begin);
+  free(runs);
+  free(kind);
+  return total;
+}

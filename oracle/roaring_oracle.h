@@ -87,6 +87,15 @@ void or_topk(const uint16_t* db, uint64_t n_rows, uint32_t dim, const uint16_t* 
 void or_topk_f32(const float* dbf, const float* norms, uint64_t n_rows, uint32_t dim,
                  const uint16_t* queries, uint32_t n_queries, const uint32_t* pass_bits, uint32_t k,
                  int metric, float* out_dist, int64_t* out_ids, int n_threads);
+/* The portable Roaring serialization (the published, library-independent
+ * "RoaringFormatSpec") of the sorted distinct ids[0..n): one container per
+ * 65536-ID chunk, typed as that format's writers do: RUN (when allow_runs)
+ * if 2 + 4*runs bytes is smaller than the alternative, else ARRAY up to 4096
+ * members, else BITMAP. Cookie 12347 with run flags when any container is a
+ * RUN (offsets only from 4 containers on), else 12346 with offsets. Returns
+ * the byte count; writes only when out != NULL and cap suffices. */
+uint64_t or_serialize_portable(const uint32_t* ids, uint64_t n, int allow_runs, uint8_t* out, uint64_t cap);
+
 void or_widen_f16(const uint16_t* src, uint64_t n, float* dst);
 void or_row_norms_f32(const float* dbf, uint64_t n_rows, uint32_t dim, float* norms);
 
