@@ -9,6 +9,7 @@
 #include <cstdint>
 #include <cstring>
 #include <string>
+#include <vector>
 
 #include "cu_roaring_b200.h"
 
@@ -85,6 +86,24 @@ void build_key_index(const uint16_t* keys, uint32_t n, uint16_t* kidx, uint32_t 
                      cudaStream_t s);
 
 int sm_count();
+
+// One container of a portable Roaring serialization (portable.cu).
+enum : uint32_t { kPortableArray = 0, kPortableBitmap = 1, kPortableRun = 2 };
+struct PortableContainer {
+  uint64_t offset;  // byte offset of the payload in the serialized buffer
+  uint32_t key;
+  uint32_t kind;    // kPortableArray / kPortableBitmap / kPortableRun
+  uint32_t count;   // ARRAY/BITMAP: cardinality; RUN: number of runs
+  uint32_t card;    // declared cardinality
+};
+struct PortableImage {
+  std::vector<PortableContainer> cs;
+  uint64_t end = 0;  // bytes of the buffer the containers use
+};
+// Checks the header of a portable Roaring serialization and locates every
+// container's payload (keys must lie below universe_size; 0 = any key).
+// Errors are raised as CR_ERR_INVALID / CR_ERR_RANGE naming `who`.
+PortableImage parse_portable(const void* data, uint64_t n_bytes, uint32_t universe_size, const char* who);
 
 // Roaring image of a flat device bitset (upload.cu): canonical container
 // types under `thr`, complement above half density, bits >= U ignored.

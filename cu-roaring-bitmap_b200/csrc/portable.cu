@@ -17,7 +17,9 @@
 // go to the device once, one block per container rebuilds its 65536-bit chunk
 // of a flat bitset, and the bitset upload builds the canonical image
 // (container types under bitmap_threshold, complement above half density).
+#include <algorithm>
 #include <cstring>
+#include <string>
 #include <vector>
 
 #include "common.cuh"
@@ -32,15 +34,7 @@ constexpr uint32_t kErrPastUniverse = 1u;
 constexpr uint32_t kErrBadRun = 2u;
 constexpr uint32_t kErrCardinality = 4u;
 
-enum : uint32_t { kKindArray = 0, kKindBitmap = 1, kKindRun = 2 };
-
-struct PortableContainer {
-  uint64_t offset;  // byte offset of the payload in the serialized buffer
-  uint32_t key;
-  uint32_t kind;
-  uint32_t count;   // ARRAY/BITMAP: cardinality; RUN: number of runs
-  uint32_t card;    // declared cardinality
-};
+enum : uint32_t { kKindArray = kPortableArray, kKindBitmap = kPortableBitmap, kKindRun = kPortableRun };
 
 __device__ __forceinline__ uint32_t ld_u16(const uint8_t* p) { return uint32_t(p[0]) | (uint32_t(p[1]) << 8); }
 
@@ -96,6 +90,9 @@ __global__ void __launch_bounds__(256) k_portable_expand(const uint8_t* buf, con
   if (threadIdx.x == 0 && s_pop != c.card) atomicOr(err, kErrCardinality);
 }
 
+}  // namespace
+
+namespace {
 struct Reader {
   const uint8_t* p;
   uint64_t n;
@@ -112,16 +109,11 @@ struct Reader {
 };
 
 }  // namespace
-}  // namespace crb
 
-using namespace crb;
-
-extern "C" int cr_upload_portable(const void* data, uint64_t n_bytes, uint32_t universe_size, cr_stream_t stream,
-                                  uint32_t bitmap_threshold, cr_gpu_roaring* out)
+PortableImage parse_portable(const void* data, uint64_t n_bytes, uint32_t universe_size, const char* who)
 {
-  CR_API_BEGIN
-  CR_REQUIRE(out != nullptr, "cr_upload_portable: null output");
-  CR_REQUIRE(data != nullptr && n_bytes >= 4, "cr_upload_portable: empty buffer");
+  const std::string w(who);
+  if (!(data != nullptr && n_bytes >= 4)) fail(CR_ERR_INVALID, w + ": empty buffer");
   const Reader rd{static_cast<const uint8_t*>(data), n_bytes};
   // Header.
   const uint32_t cookie = rd.u32(0);
@@ -137,24 +129,25 @@ extern "C" int cr_upload_portable(const void* data, uint64_t n_bytes, uint32_t u
     n = rd.u32(4);
     pos = 8;
   } else {
-    fail(CR_ERR_INVALID, "cr_upload_portable: not a portable Roaring bitmap (unknown cookie)");
+    fail(CR_ERR_INVALID, w + ": not a portable Roaring bitmap (unknown cookie)");
   }
-  CR_REQUIRE(n <= 65536, "cr_upload_portable: more than 65536 containers");
+  if (n > 65536) fail(CR_ERR_INVALID, w + ": more than 65536 containers");
   const uint64_t desc = pos;
   pos += uint64_t(n) * 4;
   const bool has_offsets = !has_runs || n >= kNoOffsetThreshold;
   const uint64_t offs = pos;
   if (has_offsets) pos += uint64_t(n) * 4;
-  CR_REQUIRE(pos <= n_bytes, "cr_upload_portable: truncated buffer");
-  const uint32_t n_chunks = n_chunks_for(universe_size);
-  std::vector<PortableContainer> cs(n);
+  if (pos > n_bytes) fail(CR_ERR_INVALID, w + ": truncated buffer");
+  const uint32_t n_chunks = universe_size ? n_chunks_for(universe_size) : 65536u;
+  PortableImage im;
+  im.cs.resize(n);
   uint64_t end = pos, cursor = pos;
   for (uint32_t i = 0; i < n; ++i) {
-    PortableContainer& c = cs[i];
+    PortableContainer& c = im.cs[i];
     c.key = rd.u16(desc + 4 * uint64_t(i));
     c.card = rd.u16(desc + 4 * uint64_t(i) + 2) + 1;
-    CR_REQUIRE(i == 0 || c.key > cs[i - 1].key, "cr_upload_portable: container keys not strictly increasing");
-    if (c.key >= n_chunks) fail(CR_ERR_RANGE, "cr_upload_portable: a container lies past universe_size");
+    if (!(i == 0 || c.key > im.cs[i - 1].key)) fail(CR_ERR_INVALID, w + ": container keys not strictly increasing");
+    if (c.key >= n_chunks) fail(CR_ERR_RANGE, w + ": a container lies past universe_size");
     const bool run = has_runs && ((rd.p[run_flags + i / 8] >> (i % 8)) & 1u);
     c.offset = has_offsets ? rd.u32(offs + 4 * uint64_t(i)) : cursor;
     uint64_t bytes;
@@ -171,10 +164,27 @@ extern "C" int cr_upload_portable(const void* data, uint64_t n_bytes, uint32_t u
       c.count = c.card;
       bytes = 8192;
     }
-    CR_REQUIRE(c.offset >= pos && c.offset + bytes <= n_bytes, "cr_upload_portable: container payload out of bounds");
+    if (!(c.offset >= pos && c.offset + bytes <= n_bytes)) fail(CR_ERR_INVALID, w + ": container payload out of bounds");
     cursor = c.offset + bytes;
     end = std::max<uint64_t>(end, cursor);
   }
+  im.end = end;
+  return im;
+}
+
+}  // namespace crb
+
+using namespace crb;
+
+extern "C" int cr_upload_portable(const void* data, uint64_t n_bytes, uint32_t universe_size, cr_stream_t stream,
+                                  uint32_t bitmap_threshold, cr_gpu_roaring* out)
+{
+  CR_API_BEGIN
+  CR_REQUIRE(out != nullptr, "cr_upload_portable: null output");
+  const PortableImage im = parse_portable(data, n_bytes, universe_size, "cr_upload_portable");
+  const std::vector<PortableContainer>& cs = im.cs;
+  const uint32_t n = uint32_t(cs.size());
+  const uint64_t end = im.end;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const uint64_t n_words = (uint64_t(universe_size) + 31) / 32;
   Scratch buf(end + sizeof(PortableContainer) * std::max<uint32_t>(n, 1) + 16 + 256, s);

@@ -35,7 +35,8 @@ EXPORTED_SYMBOLS = (
     "cr_promote_auto", "cr_deep_copy", "cr_set_operation", "cr_multi_and", "cr_multi_or",
     "cr_decompress_to_bitset", "cr_decompress_to_bitset_alloc", "cr_enumerate_ids_i64",
     "cr_enumerate_ids_u32", "cr_enumerate_ids_alloc", "cr_enumerate_ids_u32_noalloc", "cr_contains_batch", "cr_filtered_topk",
-    "cr_row_norms", "cr_topk_merge", "cr_topk_merge_packed", "cr_upload_portable", "cr_filtered_topk_check", "cr_profile_enable", "cr_profile_last_ms", "cr_profile_sum_ms",
+    "cr_row_norms", "cr_topk_merge", "cr_topk_merge_packed", "cr_upload_portable", "cr_batch_upload_portable", "cr_batch_free",
+    "cr_batch_promote", "cr_batch_multi_and", "cr_batch_decompress", "cr_batch_contains", "cr_filtered_topk_check", "cr_profile_enable", "cr_profile_last_ms", "cr_profile_sum_ms",
 )
 
 
@@ -88,6 +89,12 @@ _sigs = {
     "cr_topk_merge_packed": ([C.c_void_p, C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, _i32, C.c_void_p,
                               C.c_void_p, C.c_void_p], _i32),
     "cr_upload_portable": ([C.c_void_p, C.c_uint64, C.c_uint32, C.c_void_p, C.c_uint32, C.c_void_p], _i32),
+    "cr_batch_upload_portable": ([C.c_void_p, C.c_void_p, C.c_uint32, C.c_void_p, C.c_void_p], _i32),
+    "cr_batch_free": ([C.c_void_p], _i32),
+    "cr_batch_promote": ([C.c_void_p, C.c_void_p, C.c_void_p], _i32),
+    "cr_batch_multi_and": ([C.c_void_p, C.c_void_p, C.c_uint32, C.c_void_p, C.c_void_p], _i32),
+    "cr_batch_decompress": ([C.c_void_p, C.c_void_p, C.c_uint64, C.c_void_p], _i32),
+    "cr_batch_contains": ([C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint64, C.c_void_p, C.c_void_p], _i32),
     "cr_filtered_topk_check": ([], _i32),
     "cr_profile_sum_ms": ([_i32, C.POINTER(C.c_float), C.POINTER(C.c_uint32)], _i32),
 }
@@ -248,6 +255,84 @@ def upload_portable(data: bytes, universe_size: int, stream=None, bitmap_thresho
     buf = C.create_string_buffer(bytes(data), len(data)) if len(data) else None
     _check(_lib.cr_upload_portable(C.cast(buf, C.c_void_p) if buf is not None else None, len(data), universe_size,
                                    _stream_ptr(stream), bitmap_threshold, C.byref(out.raw)), "upload_portable")
+    return out
+
+
+class CrRoaringBatch(C.Structure):
+    """Layout of cr_roaring_batch / cu_roaring::v2::GpuRoaringBatch."""
+    _fields_ = [("n_bitmaps", C.c_uint32), ("total_containers", C.c_uint32),
+                ("n_bitmap_containers_total", C.c_uint32), ("array_pool_bytes", C.c_uint32),
+                ("run_pool_bytes", C.c_uint32), ("container_starts", C.c_void_p), ("key_index_starts", C.c_void_p),
+                ("keys", C.c_void_p), ("types", C.c_void_p), ("offsets", C.c_void_p),
+                ("cardinalities", C.c_void_p), ("key_indices", C.c_void_p), ("bitmap_data", C.c_void_p),
+                ("array_data", C.c_void_p), ("run_data", C.c_void_p),
+                ("host_total_cardinalities", C.POINTER(C.c_uint64)),
+                ("host_universe_sizes", C.POINTER(C.c_uint32)),
+                ("host_container_starts", C.POINTER(C.c_uint32)),
+                ("host_key_index_starts", C.POINTER(C.c_uint32)),
+                ("host_n_bitmap_containers", C.POINTER(C.c_uint32)),
+                ("_alloc_base", C.c_void_p), ("_host_meta_base", C.c_void_p)]
+
+
+class RoaringBatch:
+    """N bitmaps in one device block (the reference's v2 GpuRoaringBatch)."""
+
+    def __init__(self, raw: CrRoaringBatch | None = None):
+        self.raw = raw if raw is not None else CrRoaringBatch()
+
+    @property
+    def n_bitmaps(self) -> int:
+        return self.raw.n_bitmaps
+
+    def total_cardinality(self, b: int) -> int:
+        return int(self.raw.host_total_cardinalities[b])
+
+    def universe_size(self, b: int) -> int:
+        return int(self.raw.host_universe_sizes[b])
+
+    def free(self) -> None:
+        _check(_lib.cr_batch_free(C.byref(self.raw)), "batch_free")
+
+    def promote(self, stream=None) -> "RoaringBatch":
+        out = RoaringBatch()
+        _check(_lib.cr_batch_promote(C.byref(self.raw), _stream_ptr(stream), C.byref(out.raw)), "batch_promote")
+        return out
+
+    def multi_and(self, indices, stream=None) -> "RoaringBatch":
+        idx = (C.c_uint32 * len(indices))(*indices)
+        out = RoaringBatch()
+        _check(_lib.cr_batch_multi_and(C.byref(self.raw), idx, len(indices), _stream_ptr(stream), C.byref(out.raw)),
+               "batch_multi_and")
+        return out
+
+    def decompress(self, words_each: int, stream=None):
+        """[n_bitmaps, words_each] int64 (u64 words) on the device, zeroed first."""
+        torch = _torch()
+        out = torch.zeros((max(1, self.n_bitmaps), words_each), dtype=torch.int64, device="cuda")
+        _check(_lib.cr_batch_decompress(C.byref(self.raw), _dev_ptr(out), words_each, _stream_ptr(stream)),
+               "batch_decompress")
+        return out
+
+    def contains(self, bitmap_idx, ids, stream=None):
+        """bool[n]: contains(batch, bitmap_idx[i], ids[i]) (device int32 tensors)."""
+        torch = _torch()
+        n = ids.numel()
+        bits = torch.zeros(((n + 31) // 32,), dtype=torch.int32, device="cuda")
+        _check(_lib.cr_batch_contains(C.byref(self.raw), _dev_ptr(bitmap_idx), _dev_ptr(ids), n, _dev_ptr(bits),
+                                      _stream_ptr(stream)), "batch_contains")
+        shifts = torch.arange(32, device="cuda", dtype=torch.int32)
+        return ((bits[:, None] >> shifts[None, :]) & 1).flatten()[:n].bool()
+
+
+def batch_upload_portable(buffers, stream=None) -> RoaringBatch:
+    """Bitmaps in the portable Roaring serialization (list of bytes) -> a batch."""
+    n = len(buffers)
+    keep = [C.create_string_buffer(bytes(b), len(b)) for b in buffers]
+    ptrs = (C.c_void_p * max(1, n))(*[C.cast(k, C.c_void_p) for k in keep])
+    sizes = (C.c_uint64 * max(1, n))(*[len(b) for b in buffers])
+    out = RoaringBatch()
+    _check(_lib.cr_batch_upload_portable(ptrs, sizes, n, _stream_ptr(stream), C.byref(out.raw)),
+           "batch_upload_portable")
     return out
 
 

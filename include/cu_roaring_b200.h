@@ -237,6 +237,59 @@ int cr_topk_merge(const float* d_dist_parts, const int64_t* d_id_parts, uint32_t
                   uint32_t n_queries, uint32_t k, int metric, float* d_out_dist,
                   int64_t* d_out_ids, cr_stream_t stream);
 
+/* ---- Batches of bitmaps (replace the reference's v2 API,
+ * v2/include/cu_roaring_v2/api.hpp:22-69) ------------------------------------
+ * cr_roaring_batch has the exact layout of cu_roaring::v2::GpuRoaringBatch
+ * (include/cu_roaring_v2/types.cuh): N bitmaps in one device block, CSR
+ * offsets per bitmap, shared pools, no complement, host mirrors of the
+ * per-bitmap scalars. */
+typedef struct cr_roaring_batch {
+  uint32_t n_bitmaps, total_containers, n_bitmap_containers_total;
+  uint32_t array_pool_bytes, run_pool_bytes;
+  uint32_t* container_starts;
+  uint32_t* key_index_starts;
+  uint16_t* keys;
+  uint8_t* types;
+  uint32_t* offsets;
+  uint16_t* cardinalities;
+  uint16_t* key_indices;
+  uint64_t* bitmap_data;
+  uint16_t* array_data;
+  uint16_t* run_data;
+  const uint64_t* host_total_cardinalities;
+  const uint32_t* host_universe_sizes;
+  const uint32_t* host_container_starts;
+  const uint32_t* host_key_index_starts;
+  const uint32_t* host_n_bitmap_containers;
+  void* _alloc_base;
+  void* _host_meta_base;
+} cr_roaring_batch;
+
+/* N bitmaps in the portable Roaring serialization -> one batch (one device
+ * allocation, one host-to-device copy). Container types are kept as
+ * serialized. Replaces upload_batch(const roaring_bitmap_t* const*, n)
+ * (v2/include/cu_roaring_v2/api.hpp:22-25), whose CRoaring input is absent
+ * here; n == 0 gives an empty batch. */
+int cr_batch_upload_portable(const void* const* buffers, const uint64_t* sizes, uint32_t n, cr_stream_t stream,
+                             cr_roaring_batch* out);
+/* Frees both blocks of a batch and zeroes it (api.hpp:29). */
+int cr_batch_free(cr_roaring_batch* batch);
+/* Every ARRAY / RUN container of every bitmap becomes a BITMAP container
+ * (api.hpp:31-38); a new batch, the input untouched. */
+int cr_batch_promote(const cr_roaring_batch* in, cr_stream_t stream, cr_roaring_batch* out);
+/* AND of the bitmaps in[indices[0..n)) (all of them all-BITMAP), a
+ * one-bitmap batch without empty containers (api.hpp:46-55). */
+int cr_batch_multi_and(const cr_roaring_batch* in, const uint32_t* indices, uint32_t n, cr_stream_t stream,
+                       cr_roaring_batch* out);
+/* Bitmap b -> d_bitsets[b * words_each ..), u64 words (api.hpp:57-67): only
+ * the windows of present containers are written; words_each must cover
+ * every bitmap's universe. */
+int cr_batch_decompress(const cr_roaring_batch* in, uint64_t* d_bitsets, uint64_t words_each, cr_stream_t stream);
+/* Bit i of d_out_bits = contains(batch, d_bitmap_idx[i], d_ids[i]) (the
+ * query.cuh device test, run over n pairs; no reference counterpart). */
+int cr_batch_contains(const cr_roaring_batch* in, const uint32_t* d_bitmap_idx, const uint32_t* d_ids, uint64_t n,
+                      uint32_t* d_out_bits, cr_stream_t stream);
+
 /* ---- Measurement hooks (no reference counterpart) ---------------------------
  * When enabled, the library brackets its dominant kernels with CUDA events on
  * the launching stream; cr_profile_last_ms returns the device time of the

@@ -14,6 +14,8 @@
 #include <vector>
 
 #include "cu_roaring/cu_roaring.cuh"
+#include "cu_roaring_v2/api.hpp"
+#include "cu_roaring_v2/query.cuh"
 
 static int g_fail = 0, g_pass = 0;
 #define EXPECT(cond, msg)                                   \
@@ -107,6 +109,37 @@ static void check_graph_walk(const cu_roaring::GpuRoaring& bm, const std::vector
   }
   cudaFree(d_adj);
   cudaFree(d_out);
+}
+
+// Batch API (cu_roaring::v2): a user kernel testing membership through a
+// view and through the batch itself.
+__global__ void user_batch_contains(cu_roaring::v2::GpuRoaringBatch batch, cu_roaring::v2::GpuRoaringView v0,
+                                    const uint32_t* q, uint8_t* out, uint32_t n)
+{
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = uint8_t(cu_roaring::v2::contains(v0, q[i]) | (cu_roaring::v2::contains(batch, 1, q[i]) << 1));
+}
+
+// Portable serialization of sorted distinct IDs with at most 4096 per
+// 65536-ID chunk (ARRAY containers only, cookie 12346 with offsets).
+static std::vector<uint8_t> portable_arrays(const std::vector<uint32_t>& ids)
+{
+  std::vector<std::pair<uint16_t, std::vector<uint16_t>>> cs;
+  for (uint32_t x : ids) {
+    if (cs.empty() || cs.back().first != (x >> 16)) cs.push_back({uint16_t(x >> 16), {}});
+    cs.back().second.push_back(uint16_t(x & 0xFFFF));
+  }
+  std::vector<uint8_t> out;
+  auto put16 = [&](uint32_t v) { out.push_back(uint8_t(v)); out.push_back(uint8_t(v >> 8)); };
+  auto put32 = [&](uint32_t v) { put16(v & 0xFFFF); put16(v >> 16); };
+  put32(12346);
+  put32(uint32_t(cs.size()));
+  for (auto& c : cs) { put16(c.first); put16(uint32_t(c.second.size() - 1)); }
+  uint32_t off = 8 + 8 * uint32_t(cs.size());
+  for (auto& c : cs) { put32(off); off += 2 * uint32_t(c.second.size()); }
+  for (auto& c : cs)
+    for (uint16_t v : c.second) put16(v);
+  return out;
 }
 
 static std::vector<uint8_t> query(const cu_roaring::GpuRoaring& bm, const std::vector<uint32_t>& q,
@@ -273,6 +306,52 @@ int main()
     EXPECT(neg.negated, "roaring_filter: complement-stored filter");
     check_graph_walk(neg, td, 0, "roaring_filter graph walk, negated");
     gpu_roaring_free(neg);
+  }
+  {  // batch API: upload, views, contains(batch, b, id), promote, multi_and, decompress
+    std::vector<uint32_t> a, c;
+    std::vector<bool> ta(3 * 65536, false), tc(3 * 65536, false);
+    for (uint32_t i = 0; i < 3 * 65536; i += 37) { a.push_back(i); ta[i] = true; }
+    for (uint32_t i = 5; i < 3 * 65536; i += 91) { c.push_back(i); tc[i] = true; }
+    const auto sa = portable_arrays(a), sc = portable_arrays(c);
+    const void* bufs[2] = {sa.data(), sc.data()};
+    const size_t sizes[2] = {sa.size(), sc.size()};
+    auto batch = cu_roaring::v2::upload_batch_portable(bufs, sizes, 2);
+    EXPECT(batch.n_bitmaps == 2 && batch.host_total_cardinalities[0] == a.size(), "batch: upload counts");
+    std::vector<uint32_t> q(3 * 65536 + 100);
+    for (uint32_t i = 0; i < q.size(); ++i) q[i] = i;
+    uint32_t* dq = nullptr;
+    uint8_t* dout = nullptr;
+    cudaMalloc(&dq, q.size() * 4);
+    cudaMalloc(&dout, q.size());
+    cudaMemcpy(dq, q.data(), q.size() * 4, cudaMemcpyHostToDevice);
+    user_batch_contains<<<(q.size() + 255) / 256, 256>>>(batch, cu_roaring::v2::make_view(batch, 0), dq, dout,
+                                                          uint32_t(q.size()));
+    std::vector<uint8_t> got(q.size());
+    cudaMemcpy(got.data(), dout, got.size(), cudaMemcpyDeviceToHost);
+    bool ok = true;
+    for (uint32_t i = 0; i < q.size(); ++i) {
+      const bool wa = i < ta.size() && ta[i], wc = i < tc.size() && tc[i];
+      ok = ok && ((got[i] & 1) != 0) == wa && ((got[i] & 2) != 0) == wc;
+    }
+    EXPECT(ok, "batch: contains(view) and contains(batch, b, id) in a user kernel");
+    auto prom = cu_roaring::v2::promote_batch(batch);
+    const uint32_t both[2] = {0, 1};
+    auto r = cu_roaring::v2::multi_and(prom, both, 2);
+    uint64_t* dbits = nullptr;
+    cudaMalloc(&dbits, 3 * 1024 * 8);
+    cudaMemset(dbits, 0, 3 * 1024 * 8);
+    cu_roaring::v2::decompress_batch(r, dbits, 3 * 1024);
+    std::vector<uint64_t> w(3 * 1024);
+    cudaMemcpy(w.data(), dbits, w.size() * 8, cudaMemcpyDeviceToHost);
+    ok = true;
+    for (uint32_t i = 0; i < 3 * 65536; ++i) ok = ok && (((w[i >> 6] >> (i & 63)) & 1) != 0) == (ta[i] && tc[i]);
+    EXPECT(ok, "batch: promote + multi_and + decompress");
+    cudaFree(dq);
+    cudaFree(dout);
+    cudaFree(dbits);
+    cu_roaring::v2::free_batch(r);
+    cu_roaring::v2::free_batch(prom);
+    cu_roaring::v2::free_batch(batch);
   }
   {  // error convention: an ID outside the universe throws std::runtime_error
     std::vector<uint32_t> ids = {5, 500};
