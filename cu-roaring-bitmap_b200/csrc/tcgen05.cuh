@@ -156,32 +156,6 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float v[64])
   for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// Same load without the wait: several loads can be in flight before one
-// tmem_wait_ld(); the registers must not be read before that wait
-// (tmem_tie orders each use after it).
-__device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, uint32_t r[32])
-{
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-}
-
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
-// Makes every later use of r[] depend on a point after tmem_wait_ld().
-__device__ __forceinline__ void tmem_tie(uint32_t r[32])
-{
-#pragma unroll
-  for (int i = 0; i < 32; ++i) asm volatile("" : "+r"(r[i]));
-}
-
 // Shared-memory matrix descriptor for a K-major operand in the 128-byte
 // swizzled layout that a TMA SWIZZLE_128B load produces: rows of 128 bytes,
 // 8-row (1024-byte) swizzle atoms stacked at a 1024-byte stride.

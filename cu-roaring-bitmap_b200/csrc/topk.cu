@@ -1,29 +1,41 @@
 // cu_roaring B200 engine — fused filtered brute-force top-k.
 //
 // No reference counterpart (the reference only describes feeding
-// enumerate_ids into an external SDDMM, README.md:265-285). One kernel per
-// (128-query tile, database slice):
+// enumerate_ids into an external SDDMM, README.md:265-285).
 //
-//   warp 0  TMA producer: the query tile once (A operand, 32 KiB), then
-//           database tiles of 256 rows x 128 dims (B operand, 64 KiB) into a
-//           2-stage ring, both as 128-byte-swizzled K-major tiles.
-//   warp 1  one elected thread issues 8 tcgen05.mma (M=128 queries,
-//           N=256 rows, K=16 each, fp16 in, fp32 accumulate) per tile into
-//           one of two 256-column TMEM accumulators, then tcgen05.commit
-//           frees the smem stage and signals the epilogue.
-//   warps 2-5  epilogue, one thread per query (TMEM lane): for each 32-row
-//           chunk the filter word (one u32 of the shard's pass bitset) is
-//           read first; chunks with no passing row are never loaded from
-//           TMEM; passing scores are compared with the thread's running k-th
-//           best and rare survivors go to a per-query shared-memory buffer;
-//           buffers holding >= 32 entries are merged by the whole warp
-//           (bitonic sort + chunked bitonic merge) into per-query sorted
-//           top-k lists kept in global memory (L2-resident, coalesced).
+// One call (cr_filtered_topk), stream-ordered, no host wait:
+//   k_pass_words       the shard's pass bitset from the Roaring filter, with
+//                      per-256-word counts and the device total
+//   k_pass_compact     up to 3/4 pass: indices of the passing rows and a dense
+//                      copy of them (TMA-friendly); block 0 writes the plan
+//                      (SearchPlan: compacted or dense rows, tiling,
+//                      speculative rank)
+//   k_topk (prologue)  publish-only tiles: every list's best three scores
+//   k_spec             per query, the speculative bound from their union
+//   k_topk (main)      the search; rows at or above the query's bound are
+//                      appended to per-(query, list) candidate arrays
+//   k_merge            per query: radix select of the k-th best, exact rank,
+//                      verification of the speculative bound
+//   k_redo_gate        the exact per-list search, launched from the device
+//                      only when the first pass flagged it
 //
-// A second kernel merges the per-slice lists of each query (bitonic sort in
-// shared memory) and converts internal scores to distances. Internal score
-// is "larger is better": IP -> q.x; L2 -> 2 q.x - |x|^2 (distance
-// |q|^2 - score). Ties are broken toward the smaller row id.
+// k_topk, one CTA per (128-query tile, database slice), 608 threads:
+//   warp 0     TMA producer: the query tile once (A operand, 32 KiB), then
+//              database tiles of 256 rows x 128 dims (B operand, 64 KiB)
+//              into a 3-stage ring, 128-byte-swizzled K-major tiles
+//   warp 1     one thread issues 8 tcgen05.mma (M=128, N=256, K=16, fp16 in,
+//              fp32 accumulate) per tile into one of two 256-column TMEM
+//              accumulators; tcgen05.commit frees the stage and signals the
+//              epilogue
+//   warp 2     bound keeper: per query, the minimum over all lists of their
+//              published j-th best, raised to the speculative bound, in
+//              shared memory
+//   warps 3-18 epilogue, one thread per (query, quarter of each tile's
+//              rows): one 64-column TMEM load and two 32-row max trees per
+//              tile; rows at or above the bound (rare) are appended
+//
+// Internal score is "larger is better": IP -> q.x; L2 -> 2 q.x - |x|^2
+// (distance |q|^2 - score). Ties are broken toward the smaller row id.
 #include <cuda.h>
 #include <cuda_fp16.h>
 
@@ -55,7 +67,7 @@ constexpr uint32_t EPI_PARTS = EPI_WARPS / 4;          // column parts (partial 
 constexpr uint32_t PART_CHUNKS = (BN / 32) / EPI_PARTS; // 32-row chunks per part
 constexpr uint32_t EPI = EPI_WARPS * 32;
 constexpr uint32_t BUF = 64;       // candidate buffer entries per (query, half); flushed at >= 32
-constexpr uint32_t THREADS = 96 + EPI;  // producer, MMA, bound keeper, 8 epilogue warps
+constexpr uint32_t THREADS = 96 + EPI;  // producer, MMA, bound keeper, 16 epilogue warps
 constexpr uint32_t EPI_WARP0 = 3;        // first epilogue warp
 constexpr uint32_t KB_BYTES_Q = BM * 128;    // one 64-dim K-block of the query tile
 constexpr uint32_t KB_BYTES_DB = BN * 128;   // one 64-dim K-block of a database tile
@@ -378,7 +390,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       __nanosleep(p.keeper_ns);
     }
   } else {
-    // ---------------- epilogue: warps 3..10, one thread per (query, half)
+    // ---------------- epilogue: warps 3..18, one thread per (query, quarter of the rows)
     const uint32_t quarter = warp & 3u;               // TMEM lane quarter this warp may access
     const uint32_t chalf = (warp - EPI_WARP0) >> 2;   // which column part (rows of the tile)
     const uint32_t t_local = quarter * 32 + lane;     // query row inside the tile
