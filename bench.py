@@ -606,7 +606,7 @@ def main():
     cpu = None
     if rank == 0:
         if world == 1:
-            sample_rows = 1 << 20
+            sample_rows = 1 << 23  # ~10-15 s of CPU work on the box's cores
             mask_np = mask[:sample_rows].cpu().numpy()
             qps, dt, desc = cpu_topk_sample(db[:sample_rows].cpu().numpy(), q_host.numpy(),
                                             pass_words_of(mask_np), N_QUERIES, os.cpu_count() or 1)
