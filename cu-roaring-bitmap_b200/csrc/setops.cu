@@ -56,6 +56,8 @@ struct KeyPlan {
   uint8_t src;        // copy-through operand
   int src_idx;        // copy-through container
   uint32_t bound;     // payload bytes upper bound
+  uint8_t pair;       // two operands, both BITMAP here: their pool offsets below
+  uint32_t a_off, b_off;
 };
 
 __device__ __forceinline__ bool plan_key(const Operands& ops, uint32_t key, KeyPlan& kp)
@@ -91,7 +93,20 @@ __device__ __forceinline__ bool plan_key(const Operands& ops, uint32_t key, KeyP
     kp.bound = kp.type == kBitmap ? kBitmapBytes : (kp.type == kArray ? 2u * c : 4u * c);
     return true;
   }
-  kp.copy = 0; kp.src = 0; kp.src_idx = -1;
+  kp.copy = 0; kp.src = 0; kp.src_idx = -1; kp.pair = 0;
+  if (ops.np + ops.nn == 2) {
+    // Two operands both holding the key as BITMAP containers: the executor
+    // reads their words straight from these pool offsets.
+    const int ia = dev_lookup(ops.op[0], key), ib = dev_lookup(ops.op[1], key);
+    if (ia >= 0 && ib >= 0) {
+      const ContainerRef ca = dev_container(ops.op[0], ia), cb = dev_container(ops.op[1], ib);
+      if (ca.type == kBitmap && cb.type == kBitmap) {
+        kp.pair = 1;
+        kp.a_off = ca.off;
+        kp.b_off = cb.off;
+      }
+    }
+  }
   if (ops.mode == MODE_AND_SUB) {
     kp.type = any_array ? kArray : kBitmap;
     kp.bound = any_array ? 2u * min_arr : kBitmapBytes;
@@ -125,7 +140,9 @@ __global__ void __launch_bounds__(kTile) k_plan_tiles(const Operands* __restrict
   if (threadIdx.x == 0) tiles[blockIdx.x] = t;
 }
 
-// work[w] = (key | type<<16 | copy<<24, bound offset, src operand, src idx)
+// work[w] = (key | type<<16 | copy<<24, bound offset, src operand, src idx);
+// for a BITMAP pair (not copy-through): z = first operand's pool offset / 8
+// + 1, w = second's / 8 (z = 0 otherwise).
 __global__ void __launch_bounds__(kTile) k_plan_work(const Operands* __restrict__ ops_p,
                                                      const WorkTotals* tiles, uint32_t n_tiles,
                                                      uint4* work, WorkTotals* header)
@@ -159,7 +176,8 @@ __global__ void __launch_bounds__(kTile) k_plan_work(const Operands* __restrict_
     else if (kp.type == kArray) off = static_cast<uint32_t>(s_base.ab + ao);
     else off = static_cast<uint32_t>(s_base.rb + ro);
     work[s_base.n + wi] = make_uint4(key | (uint32_t(kp.type) << 16) | (uint32_t(kp.copy) << 24), off,
-                                     kp.src, static_cast<uint32_t>(kp.src_idx));
+                                     kp.pair ? (kp.a_off >> 3) + 1u : kp.src,
+                                     kp.pair ? (kp.b_off >> 3) : static_cast<uint32_t>(kp.src_idx));
   }
   if (blockIdx.x == 0 && threadIdx.x == 0) {
     header->n = s_all.n;
@@ -218,29 +236,24 @@ __global__ void __launch_bounds__(256) k_execute(const Operands* __restrict__ op
 #pragma unroll
   for (int i = 0; i < 4; ++i) acc[i] = and_sub ? ~0ull : 0ull;
   // Fast path for two operands that are both BITMAP containers here (every
-  // set_operation on promoted layouts): both operands' 16-byte loads are
-  // issued before combining, instead of waiting on one operand at a time.
+  // set_operation on promoted layouts): the planner recorded both pool
+  // offsets, so the block issues its data loads at once, with no metadata
+  // reads in front of them.
   bool done = false;
-  if (ops.np + ops.nn == 2) {
-    const int ia = dev_lookup(ops.op[0], key), ib = dev_lookup(ops.op[1], key);
-    if (ia >= 0 && ib >= 0) {
-      const ContainerRef ca = dev_container(ops.op[0], ia), cb = dev_container(ops.op[1], ib);
-      if (ca.type == kBitmap && cb.type == kBitmap) {
-        const uint4* qa = reinterpret_cast<const uint4*>(ops.op[0].bitmap + (ca.off >> 3)) + 2 * t;
-        const uint4* qb = reinterpret_cast<const uint4*>(ops.op[1].bitmap + (cb.off >> 3)) + 2 * t;
-        const uint4 a0 = __ldg(qa), a1 = __ldg(qa + 1), b0 = __ldg(qb), b1 = __ldg(qb + 1);
-        const uint64_t av[4] = {uint64_t(a0.x) | (uint64_t(a0.y) << 32), uint64_t(a0.z) | (uint64_t(a0.w) << 32),
-                                uint64_t(a1.x) | (uint64_t(a1.y) << 32), uint64_t(a1.z) | (uint64_t(a1.w) << 32)};
-        const uint64_t bv[4] = {uint64_t(b0.x) | (uint64_t(b0.y) << 32), uint64_t(b0.z) | (uint64_t(b0.w) << 32),
-                                uint64_t(b1.x) | (uint64_t(b1.y) << 32), uint64_t(b1.z) | (uint64_t(b1.w) << 32)};
-        const bool b_neg = ops.np == 1;  // ANDNOT: the second operand is subtracted
+  if (item.z != 0) {
+    const uint4* qa = reinterpret_cast<const uint4*>(ops.op[0].bitmap + (item.z - 1)) + 2 * t;
+    const uint4* qb = reinterpret_cast<const uint4*>(ops.op[1].bitmap + item.w) + 2 * t;
+    const uint4 a0 = __ldg(qa), a1 = __ldg(qa + 1), b0 = __ldg(qb), b1 = __ldg(qb + 1);
+    const uint64_t av[4] = {uint64_t(a0.x) | (uint64_t(a0.y) << 32), uint64_t(a0.z) | (uint64_t(a0.w) << 32),
+                            uint64_t(a1.x) | (uint64_t(a1.y) << 32), uint64_t(a1.z) | (uint64_t(a1.w) << 32)};
+    const uint64_t bv[4] = {uint64_t(b0.x) | (uint64_t(b0.y) << 32), uint64_t(b0.z) | (uint64_t(b0.w) << 32),
+                            uint64_t(b1.x) | (uint64_t(b1.y) << 32), uint64_t(b1.z) | (uint64_t(b1.w) << 32)};
+    const bool b_neg = ops.np == 1;  // ANDNOT: the second operand is subtracted
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-          acc[i] = b_neg ? (av[i] & ~bv[i])
-                         : (and_sub ? (av[i] & bv[i]) : (ops.mode == MODE_OR ? (av[i] | bv[i]) : (av[i] ^ bv[i])));
-        done = true;
-      }
-    }
+    for (int i = 0; i < 4; ++i)
+      acc[i] = b_neg ? (av[i] & ~bv[i])
+                     : (and_sub ? (av[i] & bv[i]) : (ops.mode == MODE_OR ? (av[i] | bv[i]) : (av[i] ^ bv[i])));
+    done = true;
   }
   for (uint32_t j = 0; j < (done ? 0u : ops.np); ++j) {
     const DevBitmap& b = ops.op[j];
