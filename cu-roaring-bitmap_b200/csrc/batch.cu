@@ -305,9 +305,12 @@ extern "C" int cr_batch_upload_portable(const void* const* buffers, const uint64
           offs[g] = uint32_t(rb);
           std::memcpy(rpool + rb, p + 2, 4 * size_t(c.count));
           uint64_t members = 0;
+          int64_t prev_last = -1;  // runs must be sorted and disjoint (the lookup bisects them)
           for (uint32_t r = 0; r < c.count; ++r) {
             const uint32_t start = p[2 + 4 * r] | (p[3 + 4 * r] << 8), len = p[4 + 4 * r] | (p[5 + 4 * r] << 8);
             CR_REQUIRE(start + len <= 0xFFFFu, "cr_batch_upload_portable: a run passes the end of its container");
+            CR_REQUIRE(int64_t(start) > prev_last, "cr_batch_upload_portable: runs not sorted and disjoint");
+            prev_last = int64_t(start) + len;
             members += len + 1;
           }
           CR_REQUIRE(members == c.card, "cr_batch_upload_portable: a container's members do not match its declared cardinality");

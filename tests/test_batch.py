@@ -48,6 +48,11 @@ def test_batch_rejects_malformed_input(built_lib, oracle):
         cr.batch_upload_portable([good, b"\x01\x02\x03\x04" + good[4:]])
     with pytest.raises(RuntimeError, match="truncated"):
         cr.batch_upload_portable([good[:9]])
+    # One RUN container holding two overlapping runs (10..19 and 15..24) that
+    # declare 20 members: sorted-and-disjoint check.
+    bad = bytes.fromhex("3b300000" "01" "00001300" "0200" "0a000900" "0f000900")
+    with pytest.raises(RuntimeError, match="disjoint"):
+        cr.batch_upload_portable([bad])
 
 
 def _sets(rng):
