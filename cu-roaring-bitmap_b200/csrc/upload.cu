@@ -417,19 +417,21 @@ __global__ void k_zero_slots(uint4* words, const uint32_t* n_slots)
 }
 
 __device__ __forceinline__ void scatter_one(uint32_t id, uint32_t U, const uint32_t* chunk_slot,
-                                            uint32_t* words, bool& bad)
+                                            uint32_t* words, bool& bad, uint32_t slot_lo, uint32_t slot_hi)
 {
   if (id >= U) { bad = true; return; }
   const uint32_t key = id >> 16;
   const uint32_t slot = chunk_slot ? __ldg(chunk_slot + key) : key;
+  if (slot < slot_lo || slot >= slot_hi) return;  // another pass's slots
   atomicOr(words + uint64_t(slot) * kChunkWords32 + ((id & 0xFFFFu) >> 5), 1u << (id & 31u));
 }
 
-// OR every ID into its chunk slot. Vector loads when the input is 16-byte
-// aligned; the result is independent of order and duplicates.
+// OR every ID whose chunk slot lies in [slot_lo, slot_hi) into that slot.
+// Vector loads when the input is 16-byte aligned; the result is independent
+// of order and duplicates.
 __global__ void __launch_bounds__(256) k_scatter(const uint32_t* ids, uint64_t n, uint32_t U,
                                                  const uint32_t* chunk_slot, uint32_t* words,
-                                                 uint32_t* err, int vec)
+                                                 uint32_t* err, int vec, uint32_t slot_lo, uint32_t slot_hi)
 {
   bool bad = false;
   const uint64_t stride = uint64_t(gridDim.x) * 256;
@@ -440,18 +442,21 @@ __global__ void __launch_bounds__(256) k_scatter(const uint32_t* ids, uint64_t n
     const uint4* p = reinterpret_cast<const uint4*>(ids);
     for (uint64_t i = tid; i < n4; i += stride) {
       const uint4 v = __ldg(p + i);
-      scatter_one(v.x, U, chunk_slot, words, bad);
-      scatter_one(v.y, U, chunk_slot, words, bad);
-      scatter_one(v.z, U, chunk_slot, words, bad);
-      scatter_one(v.w, U, chunk_slot, words, bad);
+      scatter_one(v.x, U, chunk_slot, words, bad, slot_lo, slot_hi);
+      scatter_one(v.y, U, chunk_slot, words, bad, slot_lo, slot_hi);
+      scatter_one(v.z, U, chunk_slot, words, bad, slot_lo, slot_hi);
+      scatter_one(v.w, U, chunk_slot, words, bad, slot_lo, slot_hi);
     }
     head = n4 * 4;
   }
-  for (uint64_t i = head + tid; i < n; i += stride) scatter_one(__ldg(ids + i), U, chunk_slot, words, bad);
+  for (uint64_t i = head + tid; i < n; i += stride)
+    scatter_one(__ldg(ids + i), U, chunk_slot, words, bad, slot_lo, slot_hi);
   if (__any_sync(0xFFFFFFFFu, bad) && (threadIdx.x & 31) == 0) atomicOr(err, 1u);
 }
 
 }  // namespace
+
+constexpr size_t kPassBytes = size_t(32) << 20;  // words per scatter pass (well inside L2)
 
 // Runs analyze -> plan -> (sync) -> allocate -> emit over chunk slots.
 static void build_from_chunks(const ChunkSrc& src, uint32_t max_slots, uint32_t U, uint32_t thr,
@@ -545,10 +550,22 @@ void upload_device_ids(const uint32_t* d_ids, uint64_t n, uint32_t U, uint32_t t
   src.n_words = uint64_t(max_slots) * kChunkWords32;
   src.universe = U;
   const int vec = (reinterpret_cast<uintptr_t>(d_ids) & 15u) == 0;
+  // The OR reductions go to L2; a word array much larger than L2 makes each
+  // one a DRAM read-modify-write. Above kPassBytes the IDs are streamed once
+  // per slot range of kPassBytes of words (reading the IDs again is cheaper
+  // than the missed reductions).
+  size_t pass_bytes = kPassBytes;
+  if (const char* e = getenv("CR_UPLOAD_PASS_MB")) pass_bytes = size_t(std::max(1, atoi(e))) << 20;  // measurement
+  const uint32_t slots_per_pass = std::max<uint32_t>(1u, uint32_t(pass_bytes / kBitmapBytes));
+  auto scatter_passes = [&](const uint32_t* chunk_slot) {
+    for (uint32_t lo = 0; lo < max_slots; lo += slots_per_pass)
+      k_scatter<<<grid_for(n, 8), 256, 0, s>>>(d_ids, n, U, chunk_slot, words, d_err, vec, lo,
+                                               std::min<uint64_t>(max_slots, uint64_t(lo) + slots_per_pass));
+  };
   if (dense) {
     CR_CUDA(cudaMemsetAsync(base, 0, words_b + 64, s));
     ProfileScope prof(CR_KERNEL_UPLOAD_SCATTER, s);
-    k_scatter<<<grid_for(n, 8), 256, 0, s>>>(d_ids, n, U, nullptr, words, d_err, vec);
+    scatter_passes(nullptr);
   } else {
     unsigned long long* presence = reinterpret_cast<unsigned long long*>(aux + 64);
     uint32_t* chunk_slot = reinterpret_cast<uint32_t*>(aux + 64 + 8192);
@@ -559,7 +576,7 @@ void upload_device_ids(const uint32_t* d_ids, uint64_t n, uint32_t U, uint32_t t
     k_assign_slots<<<1, 1024, 0, s>>>(presence, chunk_slot, slot_keys, n_slots);
     k_zero_slots<<<std::max(1, std::min<int>(sm_count() * 4, div_up(words_b / 16, 256))), 256, 0, s>>>(
         reinterpret_cast<uint4*>(words), n_slots);
-    k_scatter<<<grid_for(n, 8), 256, 0, s>>>(d_ids, n, U, chunk_slot, words, d_err, vec);
+    scatter_passes(chunk_slot);
     src.slot_keys = slot_keys;
     src.n_slots = n_slots;
   }
