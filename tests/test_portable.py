@@ -103,3 +103,69 @@ def test_ingest_rejects_device_side_errors(cr, oracle):
     bad[10] = 5  # container 0 declares 6 members, its payload holds 4 (plus the next header bytes)
     rc, msg = _call(cr, bytes(bad), 1 << 20)
     assert rc == -1
+
+
+def _decode_portable(b: bytes) -> np.ndarray:
+    """A pure-Python reader of the portable Roaring format, written from the
+    published specification (independent of the C writer under test)."""
+    import struct
+
+    cookie = struct.unpack_from("<I", b, 0)[0]
+    if cookie & 0xFFFF == 12347:
+        n = (cookie >> 16) + 1
+        runs = b[4:4 + (n + 7) // 8]
+        pos = 4 + (n + 7) // 8
+        is_run = [(runs[i // 8] >> (i % 8)) & 1 for i in range(n)]
+        has_off = n >= 4
+    else:
+        assert cookie == 12346
+        n = struct.unpack_from("<I", b, 4)[0]
+        pos = 8
+        is_run = [0] * n
+        has_off = True
+    hdr = [struct.unpack_from("<HH", b, pos + 4 * i) for i in range(n)]
+    pos += 4 * n
+    offs = [struct.unpack_from("<I", b, pos + 4 * i)[0] for i in range(n)] if has_off else None
+    if has_off:
+        pos += 4 * n
+    out = []
+    for i, (key, card_m1) in enumerate(hdr):
+        card = card_m1 + 1
+        at = offs[i] if offs else pos
+        if is_run[i]:
+            nr = struct.unpack_from("<H", b, at)[0]
+            pairs = np.frombuffer(b, dtype="<u2", count=2 * nr, offset=at + 2).reshape(nr, 2).astype(np.int64)
+            vals = np.concatenate([np.arange(s, s + l + 1) for s, l in pairs]) if nr else np.zeros(0, np.int64)
+            size = 2 + 4 * nr
+        elif card <= 4096:
+            vals = np.frombuffer(b, dtype="<u2", count=card, offset=at).astype(np.int64)
+            size = 2 * card
+        else:
+            words = np.frombuffer(b, dtype="<u8", count=1024, offset=at)
+            bits = np.unpackbits(words.view(np.uint8), bitorder="little")
+            vals = np.flatnonzero(bits).astype(np.int64)
+            size = 8192
+        assert vals.size == card, f"container {i}: {vals.size} members, header says {card}"
+        out.append((key << 16) + vals)
+        pos = at + size
+    return np.concatenate(out).astype(np.uint32) if out else np.zeros(0, np.uint32)
+
+
+@pytest.mark.parametrize("allow_runs", [True, False])
+def test_oracle_writer_round_trips_through_spec_reader(oracle, allow_runs):
+    rng = np.random.default_rng(17)
+    parts = []
+    for chunk in range(12):
+        base = chunk << 16
+        kind = chunk % 4
+        if kind == 0:
+            parts.append(base + rng.choice(65536, 300, replace=False))
+        elif kind == 1:
+            parts.append(base + np.flatnonzero(rng.random(65536) < 0.5))
+        elif kind == 2:
+            parts.append(base + np.arange(1000, 40000))
+        # kind 3: absent chunk
+    ids = np.unique(np.concatenate(parts)).astype(np.uint32)
+    for subset in (ids, ids[:5], ids[ids < (3 << 16)]):
+        got = _decode_portable(oracle.serialize_portable(subset, allow_runs=allow_runs))
+        assert np.array_equal(got, subset)
