@@ -105,3 +105,60 @@ def test_two_rank_sharded_topk_equals_unsharded(tmp_path, metric, built_lib):
     want_d, want_i = oracle.topk(db, qs, k, metric, _words(keep))
     assert np.array_equal(got["i"], want_i)
     np.testing.assert_allclose(got["d"], want_d, rtol=1e-5)
+
+
+def _packed_worker(rank, world, port, k, metric, result_path):
+    """Each rank writes its shard's top-k into the packed send block (fp32
+    distances, then int64 ids), gathers the blocks to rank 0 in one
+    collective, and rank 0 reads the views back out of the gathered bytes:
+    the same exchange bench.py runs over NCCL, here over gloo."""
+    import sys
+    from pathlib import Path
+
+    repo = Path(__file__).resolve().parent.parent
+    for p in (repo / "cu-roaring-bitmap_b200", repo / "oracle"):
+        sys.path.insert(0, str(p))
+    import oracle
+    from cu_roaring_b200 import shard_range, topk_packed_buffer  # noqa: E402
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    db, qs, keep = _data()
+    nq = qs.shape[0]
+    lo, hi = shard_range(db.shape[0], rank, world)
+    d, i = oracle.topk(db[lo:hi], qs, k, metric, _words(keep[lo:hi]))
+    block, bd, bi = topk_packed_buffer(nq, k, "cpu")
+    bd.copy_(torch.from_numpy(d))
+    bi.copy_(torch.from_numpy(np.where(i >= 0, i + lo, -1)))
+    gathered = torch.empty((world, block.numel()), dtype=torch.uint8)
+    dist.gather(block, gather_list=list(gathered.unbind(0)) if rank == 0 else None, dst=0)
+    if rank == 0:
+        nd = nq * k
+        gd = gathered[:, : nd * 4].contiguous().view(torch.float32).view(world, nq, k)
+        gi = gathered[:, nd * 4:].contiguous().view(torch.int64).view(world, nq, k)
+        md, mi = merge_lists(gd.numpy(), gi.numpy(), k, metric)
+        np.savez(result_path, d=md, i=mi)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("metric", [0, 1])
+def test_two_rank_packed_gather_equals_unsharded(tmp_path, metric, built_lib):
+    pytest.importorskip("torch.distributed")
+    import sys
+    from pathlib import Path
+
+    repo = Path(__file__).resolve().parent.parent
+    sys.path.insert(0, str(repo / "oracle"))
+    import oracle
+
+    if "cu_roaring_b200" not in sys.modules:
+        pytest.importorskip("cu_roaring_b200")
+    k, world = 20, 2
+    out = tmp_path / "merged.npz"
+    mp.spawn(_packed_worker, args=(world, _free_port(), k, metric, str(out)), nprocs=world, join=True)
+    got = np.load(out)
+    db, qs, keep = _data()
+    want_d, want_i = oracle.topk(db, qs, k, metric, _words(keep))
+    assert np.array_equal(got["i"], want_i)
+    np.testing.assert_allclose(got["d"], want_d, rtol=1e-5)
