@@ -421,7 +421,7 @@ def secondary_metrics(torch, cr, pk):
     up["from_device_bitset_AUTO"] = {"ms": t * 1e3, "GBps_bitset_read": U / 8 / t / 1e9}
     del words
     out["upload_c2"] = {"n_ids": n_ids, "universe": U, **up,
-                        "note": "API time incl. its one host sync; generators give ~3e8 IDs (see SURVEY 8d)"}
+                        "note": "API time incl. its one host sync; generators give ~3e8 IDs"}
     # ---- config 3: multi_and over 3 / 5 / 8 predicates, to_csr of the result
     bms = []
     for p_ in (0.5, 0.1, 0.01, 0.001):
