@@ -86,6 +86,20 @@ void build_key_index(const uint16_t* keys, uint32_t n, uint16_t* kidx, uint32_t 
                      cudaStream_t s);
 
 int sm_count();
+// Raises the dynamic shared memory limit of `fn` on the current device.
+// Function attributes are per device, so every device a process launches on
+// gets its own call; later calls on that device are free.
+void set_max_dynamic_smem(const void* fn, int bytes);
+
+// The fused filtered top-k of one shard (topk.cu), stream-ordered, and the
+// merge of per-shard lists that sit at fixed strides (elements) apart.
+void filtered_topk_enqueue(const uint16_t* d_db, const float* d_db_norms, uint64_t n_rows, uint32_t dim,
+                           const uint16_t* d_queries, uint32_t n_queries, const cr_gpu_roaring* filter,
+                           uint64_t row_offset, uint32_t k, int metric, float* d_out_dist, int64_t* d_out_ids,
+                           cudaStream_t s);
+void topk_merge_enqueue(const float* d_dist, const int64_t* d_ids, uint64_t dist_stride, uint64_t id_stride,
+                        uint32_t n_parts, uint32_t n_queries, uint32_t k, int metric, float* d_out_dist,
+                        int64_t* d_out_ids, cudaStream_t s);
 
 // One container of a portable Roaring serialization (portable.cu).
 enum : uint32_t { kPortableArray = 0, kPortableBitmap = 1, kPortableRun = 2 };

@@ -1,7 +1,9 @@
 // cu_roaring B200 engine — errors, packed allocation, device queries, free,
 // deep copy, threshold resolution.
+#include <map>
 #include <mutex>
 #include <vector>
+
 
 #include "common.cuh"
 
@@ -109,6 +111,19 @@ int sm_count()
   CR_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
   if (dev < 64) cached[dev] = n;
   return n;
+}
+
+void set_max_dynamic_smem(const void* fn, int bytes)
+{
+  static std::mutex mu;
+  static std::map<std::pair<int, const void*>, int> done;
+  int dev = 0;
+  CR_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(mu);
+  int& have = done[{dev, fn}];
+  if (have >= bytes) return;
+  CR_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  have = bytes;
 }
 
 uint64_t l2_bytes(int device)

@@ -8,6 +8,8 @@
 // enumerate_ids: count -> tile scan -> one CTA per unit writes sorted IDs;
 // negated bitmaps enumerate the complement (the reference ignores
 // `negated`, src/to_csr.cu:36-131).
+#include <cuda.h>
+
 #include <algorithm>
 #include <mutex>
 #include <string>
@@ -430,16 +432,32 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch
 
 // Device address of g_noalloc_scratch on the current device. The first call
 // on each device resolves it with cudaGetSymbolAddress (with that device
-// current); later calls reuse the cached address.
+// current); later calls reuse the cached address as long as the device's
+// context is the same one. A context created anew (after cudaDeviceReset, or
+// a release and re-creation of the primary context) reloads the module, so
+// its address is looked up again.
 static unsigned char* noalloc_scratch()
 {
+  using CtxGetCurrentFn = CUresult (*)(CUcontext*);
   static std::mutex mu;
   static unsigned char* addr[64] = {};
+  static CUcontext ctx_of[64] = {};
+  static CtxGetCurrentFn ctx_get = nullptr;
   int dev = 0;
   CR_CUDA(cudaGetDevice(&dev));
   CR_REQUIRE(dev >= 0 && dev < 64, "cr_enumerate_ids_u32_noalloc: device ordinal out of range");
   std::lock_guard<std::mutex> lock(mu);
-  if (!addr[dev]) {
+  if (!ctx_get) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || fn == nullptr)
+      fail(CR_ERR_CUDA, "cr_enumerate_ids_u32_noalloc: cuCtxGetCurrent is not available");
+    ctx_get = reinterpret_cast<CtxGetCurrentFn>(fn);
+  }
+  CUcontext ctx = nullptr;
+  if (ctx_get(&ctx) != CUDA_SUCCESS) fail(CR_ERR_CUDA, "cr_enumerate_ids_u32_noalloc: cuCtxGetCurrent failed");
+  if (!addr[dev] || ctx == nullptr || ctx_of[dev] != ctx) {
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess || p == nullptr) {
@@ -448,6 +466,9 @@ static unsigned char* noalloc_scratch()
                             cudaGetErrorString(e));
     }
     addr[dev] = static_cast<unsigned char*>(p);
+    // The lookup made the device's context current if nothing had yet.
+    if (ctx == nullptr && ctx_get(&ctx) != CUDA_SUCCESS) ctx = nullptr;
+    ctx_of[dev] = ctx;
   }
   return addr[dev];
 }

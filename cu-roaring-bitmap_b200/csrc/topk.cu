@@ -1350,11 +1350,8 @@ void merge_launch(const float* ps, const int64_t* pid, uint32_t parts, uint32_t 
   // (elements; default: parts packed back to back as [parts][nq][k]).
   if (!s_stride) s_stride = uint64_t(nq) * k;
   if (!i_stride) i_stride = uint64_t(nq) * k;
-  static std::once_flag once;
   const size_t smem = MERGE_N * 12;
-  std::call_once(once, [&] {
-    cudaFuncSetAttribute(k_merge, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-  });
+  set_max_dynamic_smem(reinterpret_cast<const void*>(k_merge), int(smem));
   ProfileScope prof(CR_KERNEL_TOPK_MERGE, s);
   k_merge<<<nq, MERGE_THREADS, smem, s>>>(ps, pid, parts, nq, k, metric, kind, queries, dim, od, oi,
                                           cand_cnt, cap, cand_r, row_map, row_offset, pub, n_lists, n_rows,
@@ -1561,11 +1558,8 @@ static void run_search(const SearchInput& in, const uint16_t* d_queries, uint32_
                        bool allow_append, bool allow_spec, const uint32_t* guard, uint32_t* err,
                        bool* used_append)
 {
-  static std::once_flag once;
-  std::call_once(once, [] {
-    cudaFuncSetAttribute(k_topk<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(SMEM_TOTAL));
-    cudaFuncSetAttribute(k_topk<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(SMEM_TOTAL));
-  });
+  set_max_dynamic_smem(reinterpret_cast<const void*>(k_topk<true>), int(SMEM_TOTAL));
+  set_max_dynamic_smem(reinterpret_cast<const void*>(k_topk<false>), int(SMEM_TOTAL));
   // Grid: query tiles x slices, sized for the largest plan (every shard row).
   const uint32_t max_tiles = std::max<uint32_t>(1u, div_up(in.shard_rows, BN));
   const uint32_t qtiles = div_up(n_queries, BM);
@@ -1677,13 +1671,13 @@ static void run_search(const SearchInput& in, const uint16_t* d_queries, uint32_
   }
 }
 
-extern "C" int cr_filtered_topk(const uint16_t* d_db, const float* d_db_norms, uint64_t n_rows,
-                                uint32_t dim, const uint16_t* d_queries, uint32_t n_queries,
-                                const cr_gpu_roaring* filter, uint64_t row_offset, uint32_t k,
-                                int metric, float* d_out_dist, int64_t* d_out_ids,
-                                cr_stream_t stream)
+namespace crb {
+
+void filtered_topk_enqueue(const uint16_t* d_db, const float* d_db_norms, uint64_t n_rows, uint32_t dim,
+                           const uint16_t* d_queries, uint32_t n_queries, const cr_gpu_roaring* filter,
+                           uint64_t row_offset, uint32_t k, int metric, float* d_out_dist, int64_t* d_out_ids,
+                           cudaStream_t s)
 {
-  CR_API_BEGIN
   CR_REQUIRE(dim == DIM, "cr_filtered_topk: this build supports dim == 128");
   CR_REQUIRE(k >= 1 && k <= 256, "cr_filtered_topk: k must be in [1, 256]");
   CR_REQUIRE(metric == CR_METRIC_IP || metric == CR_METRIC_L2, "cr_filtered_topk: unknown metric");
@@ -1694,7 +1688,6 @@ extern "C" int cr_filtered_topk(const uint16_t* d_db, const float* d_db_norms, u
                  (reinterpret_cast<uintptr_t>(d_queries) & 15u) == 0,
              "cr_filtered_topk: db and queries must be 16-byte aligned");
   ErrorRing::get().check(false);  // failures of earlier searches on this thread
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const bool l2 = metric == CR_METRIC_L2;
   Trace& tr = Trace::get();
   tr.on = getenv("CR_TOPK_TRACE") != nullptr;
@@ -1797,6 +1790,28 @@ extern "C" int cr_filtered_topk(const uint16_t* d_db, const float* d_db_norms, u
   ErrorRing::get().record(err0, appended ? err1 : nullptr, s);
   tr.mark("search", s);
   tr.print();
+}
+
+void topk_merge_enqueue(const float* d_dist, const int64_t* d_ids, uint64_t dist_stride, uint64_t id_stride,
+                        uint32_t n_parts, uint32_t n_queries, uint32_t k, int metric, float* d_out_dist,
+                        int64_t* d_out_ids, cudaStream_t s)
+{
+  merge_launch(d_dist, d_ids, n_parts, n_queries, k, metric, 1, nullptr, 0, d_out_dist, d_out_ids, s, nullptr, 0,
+               nullptr, nullptr, 0, nullptr, 0, 0, nullptr, nullptr, nullptr, nullptr, dist_stride, id_stride);
+}
+
+}  // namespace crb
+
+
+extern "C" int cr_filtered_topk(const uint16_t* d_db, const float* d_db_norms, uint64_t n_rows,
+                                uint32_t dim, const uint16_t* d_queries, uint32_t n_queries,
+                                const cr_gpu_roaring* filter, uint64_t row_offset, uint32_t k,
+                                int metric, float* d_out_dist, int64_t* d_out_ids,
+                                cr_stream_t stream)
+{
+  CR_API_BEGIN
+  filtered_topk_enqueue(d_db, d_db_norms, n_rows, dim, d_queries, n_queries, filter, row_offset, k, metric,
+                        d_out_dist, d_out_ids, reinterpret_cast<cudaStream_t>(stream));
   CR_API_END
 }
 

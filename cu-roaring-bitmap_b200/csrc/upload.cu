@@ -431,8 +431,12 @@ __device__ __forceinline__ void scatter_one(uint32_t id, uint32_t U, const uint3
 // of order and duplicates.
 __global__ void __launch_bounds__(256) k_scatter(const uint32_t* ids, uint64_t n, uint32_t U,
                                                  const uint32_t* chunk_slot, uint32_t* words,
-                                                 uint32_t* err, int vec, uint32_t slot_lo, uint32_t slot_hi)
+                                                 uint32_t* err, int vec, uint32_t slot_lo, uint32_t slot_hi,
+                                                 const uint32_t* n_slots)
 {
+  // Sparse inputs size their passes by the host bound min(n, chunks); a pass
+  // whose slot range starts past the slots actually used has nothing to do.
+  if (n_slots && slot_lo >= *n_slots) return;
   bool bad = false;
   const uint64_t stride = uint64_t(gridDim.x) * 256;
   const uint64_t tid = uint64_t(blockIdx.x) * 256 + threadIdx.x;
@@ -554,18 +558,17 @@ void upload_device_ids(const uint32_t* d_ids, uint64_t n, uint32_t U, uint32_t t
   // one a DRAM read-modify-write. Above kPassBytes the IDs are streamed once
   // per slot range of kPassBytes of words (reading the IDs again is cheaper
   // than the missed reductions).
-  size_t pass_bytes = kPassBytes;
-  if (const char* e = getenv("CR_UPLOAD_PASS_MB")) pass_bytes = size_t(std::max(1, atoi(e))) << 20;  // measurement
-  const uint32_t slots_per_pass = std::max<uint32_t>(1u, uint32_t(pass_bytes / kBitmapBytes));
-  auto scatter_passes = [&](const uint32_t* chunk_slot) {
+  const uint32_t slots_per_pass = std::max<uint32_t>(1u, uint32_t(kPassBytes / kBitmapBytes));
+  auto scatter_passes = [&](const uint32_t* chunk_slot, const uint32_t* n_slots) {
     for (uint32_t lo = 0; lo < max_slots; lo += slots_per_pass)
       k_scatter<<<grid_for(n, 8), 256, 0, s>>>(d_ids, n, U, chunk_slot, words, d_err, vec, lo,
-                                               std::min<uint64_t>(max_slots, uint64_t(lo) + slots_per_pass));
+                                               std::min<uint64_t>(max_slots, uint64_t(lo) + slots_per_pass),
+                                               n_slots);
   };
   if (dense) {
     CR_CUDA(cudaMemsetAsync(base, 0, words_b + 64, s));
     ProfileScope prof(CR_KERNEL_UPLOAD_SCATTER, s);
-    scatter_passes(nullptr);
+    scatter_passes(nullptr, nullptr);
   } else {
     unsigned long long* presence = reinterpret_cast<unsigned long long*>(aux + 64);
     uint32_t* chunk_slot = reinterpret_cast<uint32_t*>(aux + 64 + 8192);
@@ -576,7 +579,7 @@ void upload_device_ids(const uint32_t* d_ids, uint64_t n, uint32_t U, uint32_t t
     k_assign_slots<<<1, 1024, 0, s>>>(presence, chunk_slot, slot_keys, n_slots);
     k_zero_slots<<<std::max(1, std::min<int>(sm_count() * 4, div_up(words_b / 16, 256))), 256, 0, s>>>(
         reinterpret_cast<uint4*>(words), n_slots);
-    scatter_passes(chunk_slot);
+    scatter_passes(chunk_slot, n_slots);
     src.slot_keys = slot_keys;
     src.n_slots = n_slots;
   }

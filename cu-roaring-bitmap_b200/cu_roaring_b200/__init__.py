@@ -37,6 +37,8 @@ EXPORTED_SYMBOLS = (
     "cr_enumerate_ids_u32", "cr_enumerate_ids_alloc", "cr_enumerate_ids_u32_noalloc", "cr_contains_batch", "cr_filtered_topk",
     "cr_row_norms", "cr_topk_merge", "cr_topk_merge_packed", "cr_upload_portable", "cr_batch_upload_portable", "cr_batch_free",
     "cr_batch_promote", "cr_batch_multi_and", "cr_batch_decompress", "cr_batch_contains", "cr_filtered_topk_check", "cr_profile_enable", "cr_profile_last_ms", "cr_profile_sum_ms",
+    "cr_topk_comm_unique_id", "cr_topk_comm_init", "cr_topk_comm_size", "cr_topk_comm_destroy",
+    "cr_filtered_topk_sharded",
 )
 
 
@@ -97,6 +99,12 @@ _sigs = {
     "cr_batch_contains": ([C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint64, C.c_void_p, C.c_void_p], _i32),
     "cr_filtered_topk_check": ([], _i32),
     "cr_profile_sum_ms": ([_i32, C.POINTER(C.c_float), C.POINTER(C.c_uint32)], _i32),
+    "cr_topk_comm_unique_id": ([_vp, _u32], _i32),
+    "cr_topk_comm_init": ([_vp, _i32, _i32, C.POINTER(_vp)], _i32),
+    "cr_topk_comm_size": ([_vp, C.POINTER(_i32), C.POINTER(_i32)], _i32),
+    "cr_topk_comm_destroy": ([_vp], _i32),
+    "cr_filtered_topk_sharded": ([_vp, _i32, _vp, _vp, _u64, _u32, _vp, _u32, _P, _u64, _u32, _i32, _vp, _vp,
+                                  _vp], _i32),
 }
 for _name, (_args, _res) in _sigs.items():
     _f = getattr(_lib, _name)
@@ -501,6 +509,57 @@ def topk_merge_packed(blocks, n_queries: int, k: int, metric: int = METRIC_IP, s
     _check(_lib.cr_topk_merge_packed(_dev_ptr(blocks), blocks.stride(0), p, n_queries, k, metric,
                                      _dev_ptr(out_d), _dev_ptr(out_i), _stream_ptr(stream)), "topk_merge_packed")
     return out_d, out_i
+
+
+# ------------------------------------------------- row-sharded top-k (NCCL)
+
+TOPK_COMM_ID_BYTES = 128
+
+
+def topk_comm_unique_id() -> bytes:
+    """Rank 0 makes the communicator's id; hand it to every rank."""
+    buf = C.create_string_buffer(TOPK_COMM_ID_BYTES)
+    _check(_lib.cr_topk_comm_unique_id(buf, TOPK_COMM_ID_BYTES), "topk_comm_unique_id")
+    return buf.raw
+
+
+class TopkComm:
+    """The communicator of cr_filtered_topk_sharded (one per rank; every
+    rank constructs it together, with its own GPU current)."""
+
+    def __init__(self, unique_id: bytes, n_ranks: int, rank: int):
+        if len(unique_id) != TOPK_COMM_ID_BYTES:
+            raise ValueError("unique_id must be TOPK_COMM_ID_BYTES bytes")
+        self.handle = C.c_void_p()
+        _check(_lib.cr_topk_comm_init(C.c_char_p(unique_id), n_ranks, rank, C.byref(self.handle)),
+               "topk_comm_init")
+        self.n_ranks, self.rank = n_ranks, rank
+
+    def destroy(self) -> None:
+        if self.handle:
+            _check(_lib.cr_topk_comm_destroy(self.handle), "topk_comm_destroy")
+            self.handle = C.c_void_p()
+
+
+def filtered_topk_sharded(comm: TopkComm, db, queries, k: int, metric: int = METRIC_IP,
+                          filter: GpuRoaring | None = None, db_norms=None, row_offset: int = 0, root: int = 0,
+                          stream=None, out_dist=None, out_ids=None):
+    """This rank's rows `db` (global row IDs from row_offset) searched and the
+    per-rank lists merged on `root`. Returns (dist, ids) on the root, None
+    elsewhere."""
+    torch = _torch()
+    q = queries.shape[0]
+    is_root = comm.rank == root
+    if is_root and out_dist is None:
+        out_dist = torch.empty((q, k), dtype=torch.float32, device=db.device)
+    if is_root and out_ids is None:
+        out_ids = torch.empty((q, k), dtype=torch.int64, device=db.device)
+    _check(_lib.cr_filtered_topk_sharded(
+        comm.handle, root, _dev_ptr(db), _dev_ptr(db_norms) if db_norms is not None else None, db.shape[0],
+        db.shape[1], _dev_ptr(queries), q, C.byref(filter.raw) if filter is not None else None, row_offset, k,
+        metric, _dev_ptr(out_dist) if is_root else None, _dev_ptr(out_ids) if is_root else None,
+        _stream_ptr(stream)), "filtered_topk_sharded")
+    return (out_dist, out_ids) if is_root else None
 
 
 # ------------------------------------------------------------- measurement

@@ -61,7 +61,8 @@ typedef enum cr_status {
   CR_ERR_OOM         = -3, /* device allocation failed                          */
   CR_ERR_RANGE       = -4, /* an input ID is >= universe_size                   */
   CR_ERR_DEVICE      = -5, /* a kernel raised its device-side error flag        */
-  CR_ERR_UNSUPPORTED = -6  /* configuration not supported by this build         */
+  CR_ERR_UNSUPPORTED = -6, /* configuration not supported by this build         */
+  CR_ERR_COMM        = -7  /* a collective between ranks failed (NCCL)         */
 } cr_status;
 
 /* Promotion thresholds (reference include/cu_roaring/detail/promote.cuh:38-40). */
@@ -167,7 +168,7 @@ int cr_enumerate_ids_alloc(const cr_gpu_roaring* bm, cr_stream_t stream, int64_t
  * reference). For callers that must not allocate device memory while they
  * run, e.g. a server that gave all GPU memory to its own pool at start-up or
  * a latency-critical path that forbids allocator calls. Its scratch is one
- * fixed array of about 0.9 MiB inside the library, resident on every GPU that
+ * fixed array of 918,016 bytes (0.875 MiB) inside the library, resident on every GPU that
  * loads it; it covers any valid bitmap (at most 65536 containers/chunks) and
  * larger inputs are rejected with CR_ERR_INVALID. The first call on a device
  * looks up that array's device address; make that first call before any
@@ -226,6 +227,35 @@ int cr_topk_merge_packed(const void* d_parts, uint64_t part_bytes, uint32_t n_pa
 /* Waits for this host thread's outstanding cr_filtered_topk searches and
  * returns CR_ERR_DEVICE if any of them failed on the device. */
 int cr_filtered_topk_check(void);
+
+/* ---- Row-sharded top-k over several GPUs (no reference counterpart: the
+ * reference has neither a top-k nor a multi-GPU path) ------------------------
+ * One process (rank) per GPU. A communicator is made once per rank:
+ * rank 0 calls cr_topk_comm_unique_id, hands the CR_TOPK_COMM_ID_BYTES bytes
+ * to every rank by any host channel, and every rank calls cr_topk_comm_init
+ * with its device current (all ranks together: the call waits for the
+ * others). NCCL is loaded at run time; without it these calls return
+ * CR_ERR_UNSUPPORTED. */
+#define CR_TOPK_COMM_ID_BYTES 128
+typedef struct cr_topk_comm_st* cr_topk_comm;
+int cr_topk_comm_unique_id(void* out_id, uint32_t n_bytes);
+int cr_topk_comm_init(const void* unique_id, int n_ranks, int rank, cr_topk_comm* out);
+int cr_topk_comm_size(cr_topk_comm comm, int* n_ranks, int* rank);
+/* Waits for the device, frees the communicator and its gather buffer. */
+int cr_topk_comm_destroy(cr_topk_comm comm);
+
+/* Every rank calls this with its own rows [row_offset, row_offset +
+ * shard_rows) of the database (d_db holds just those rows) and the same
+ * queries, filter, k and metric. Each rank searches its rows like
+ * cr_filtered_topk (filter queried with global row IDs, output IDs global);
+ * the per-rank [n_queries x k] lists go to `root` in one NCCL group of
+ * point-to-point transfers and the root writes the merged top-k to
+ * d_out_dist / d_out_ids (the other ranks' output pointers are not used and
+ * may be NULL). Stream-ordered on every rank, no host wait. */
+int cr_filtered_topk_sharded(cr_topk_comm comm, int root, const uint16_t* d_db, const float* d_db_norms,
+                             uint64_t shard_rows, uint32_t dim, const uint16_t* d_queries, uint32_t n_queries,
+                             const cr_gpu_roaring* filter, uint64_t row_offset, uint32_t k, int metric,
+                             float* d_out_dist, int64_t* d_out_ids, cr_stream_t stream);
 
 /* Squared L2 norms of fp16 rows (fp32 accumulate) for the L2 metric. */
 int cr_row_norms(const uint16_t* d_db, uint64_t n_rows, uint32_t dim, float* d_out,

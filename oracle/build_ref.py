@@ -7,12 +7,15 @@ is provided (oracle/_ref/shim/roaring/roaring.h, written by this script) for
 the one header (detail/upload.cuh) that names it in signatures."""
 from __future__ import annotations
 
+import os
 import subprocess
 import sys
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
-REF = Path("/root/reference")
+# The reference checkout: first argument, else CU_ROARING_REFERENCE, else the
+# default location of the read-only checkout.
+REF = Path(sys.argv[1] if len(sys.argv) > 1 else os.environ.get("CU_ROARING_REFERENCE", "/root/reference"))
 OUT = HERE / "_ref"
 LIB = OUT / "libref_cu_roaring.so"
 SOURCES = ["src/upload_ids.cu", "src/promote.cu", "src/set_ops.cu", "src/decompress.cu", "src/to_csr.cu"]

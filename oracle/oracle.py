@@ -19,7 +19,7 @@ LIB = HERE / "liboracle.so"
 
 
 def build() -> Path:
-    src = [HERE / "roaring_oracle.c", HERE / "roaring_oracle.h"]
+    src = [HERE / "roaring_oracle.c", HERE / "roaring_oracle.h", HERE / "cpu_upload.cpp", HERE / "Makefile"]
     if not LIB.exists() or LIB.stat().st_mtime < max(p.stat().st_mtime for p in src):
         subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
     return LIB
@@ -66,6 +66,7 @@ def lib():
             "or_topk_f32": ([v, v, u64, u32, v, u32, v, u32, i32, v, v, i32], None),
             "or_widen_f16": ([v, u64, v], None),
             "or_row_norms_f32": ([v, u64, u32, v], None),
+            "or_cpu_upload_sorted": ([v, u64, u32, u32, v], u64),
         }
         for name, (a, r) in sig.items():
             f = getattr(_lib, name)
@@ -160,6 +161,16 @@ def from_bitset(words, universe: int, threshold: int = 0xFFFFFFFF, l2_bytes: int
     lib().or_from_bitset(words.ctypes.data if words.size else None, words.size, universe, threshold,
                          l2_bytes, C.byref(b.im))
     return b
+
+
+def cpu_upload_sorted(ids, universe: int, threshold: int) -> dict:
+    """The reference's host upload path restated (sort, unique, complement,
+    partition, pools); CPU baseline timing only. Returns its counts."""
+    ids = np.ascontiguousarray(ids, dtype=np.uint32)
+    cnt = np.zeros(4, dtype=np.uint64)
+    lib().or_cpu_upload_sorted(ids.ctypes.data if ids.size else None, ids.size, universe, threshold,
+                               cnt.ctypes.data)
+    return {"containers": int(cnt[0]), "bitmaps": int(cnt[1]), "arrays": int(cnt[2]), "cardinality": int(cnt[3])}
 
 
 def set_operation(a: OracleBitmap, b: OracleBitmap, op: int) -> OracleBitmap:

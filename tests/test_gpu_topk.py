@@ -24,24 +24,9 @@ def make_data(n, q, dim=128, seed=0):
 
 
 def check_topk(d_gpu, i_gpu, d_ref, i_ref, metric):
-    k = d_ref.shape[1]
-    valid = i_ref >= 0
-    assert np.array_equal(valid, i_gpu >= 0), "number of results differs"
-    scale = np.maximum(np.abs(d_ref), 1e-3)
-    diff = np.abs(np.where(valid, d_gpu - d_ref, 0.0))
-    assert (diff <= RTOL * scale + 1e-6).all(), f"max distance error {diff.max()}"
-    for qi in range(d_ref.shape[0]):
-        a = set(i_gpu[qi][valid[qi]].tolist())
-        b = set(i_ref[qi][valid[qi]].tolist())
-        if a == b:
-            continue
-        kth = d_ref[qi][valid[qi]][-1]
-        # Only boundary ties may differ.
-        for r in a ^ b:
-            pos = np.flatnonzero(i_gpu[qi] == r)
-            dist = d_gpu[qi][pos[0]] if pos.size else d_ref[qi][np.flatnonzero(i_ref[qi] == r)[0]]
-            assert abs(dist - kth) <= RTOL * max(abs(kth), 1e-3) + 1e-6, f"query {qi}: id {r}"
-    _ = k
+    from checks import check_topk as _check
+
+    _check(d_gpu, i_gpu, d_ref, i_ref, f"metric {metric}")
 
 
 @pytest.fixture(scope="module")
