@@ -840,6 +840,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-secondary", action="store_true")
+    ap.add_argument("--secondary", default="all", choices=["all", "topk", "roaring", "none"],
+                    help="which secondary measurements run at N=1 (all by default)")
     ap.add_argument("--rows", type=int, default=N_ROWS, help="database rows (profiling runs only)")
     args = ap.parse_args()
     if args.impl == "reference":
@@ -984,12 +986,15 @@ def main():
                                             pass_words_of(mask_np), N_QUERIES, threads)
             cpu = {"value": qps, "unit": "queries/s", "cores": threads, "kind": "port",
                    "sample": desc, "seconds": dt}
-        if not args.no_secondary and world == 1:
-            sweep = topk_sweep(torch, cr, db, queries, tags_local, pk, fails)
+        which = "none" if args.no_secondary else args.secondary
+        if which != "none" and world == 1:
+            secondary = {}
+            if which in ("all", "topk"):
+                secondary["topk_sweep"] = topk_sweep(torch, cr, db, queries, tags_local, pk, fails)
             del db
             torch.cuda.empty_cache()
-            secondary = secondary_metrics(torch, cr, pk, fails, threads)
-            secondary["topk_sweep"] = sweep
+            if which in ("all", "roaring"):
+                secondary.update(secondary_metrics(torch, cr, pk, fails, threads))
 
     if rank == 0:
         rows_local = hi - lo

@@ -100,6 +100,7 @@ struct TopkParams {
   const uint32_t* pass;  // shard pass bitset (dense plans; null = every row passes)
   const float* norms;    // squared shard row norms (L2, dense plans)
   const float* comp_norms;  // squared norms of the compacted rows (L2, compacted plans)
+  const float* chunk_min;   // L2: least squared norm of each 32-row chunk of the searched rows
   const uint32_t* guard; // non-null: run only if this error word has kErrOverflow/kErrSpec set
   uint32_t spec_capable; // the prologue launch and k_spec run before this search
   float* list_s;         // per-query sorted lists: [cta][BM][2][k]
@@ -252,7 +253,7 @@ __device__ __forceinline__ float pick32(const float* v, uint32_t j)
   return a[0];
 }
 
-template <bool APPEND>
+template <bool APPEND, bool L2>
 __global__ void __launch_bounds__(THREADS, 1)
     k_topk(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tdb,
            const __grid_constant__ CUtensorMap tdb_comp, TopkParams p)
@@ -405,7 +406,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint32_t* mybuf_r = buf_r + e_local * BUF;
     uint32_t half = 0, cnt = 0, nb = 0, thr_r = 0xFFFFFFFFu;
     float thr_s = -INFINITY;
-    const bool l2 = p.metric == CR_METRIC_L2;
+    constexpr bool l2 = L2;  // the metric is a template parameter: IP code carries no L2 work
 
     // Warp-cooperative merge of every lane whose buffer holds >= `min_fill`.
     auto flush = [&](uint32_t min_fill) {
@@ -479,6 +480,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_after();
       const uint32_t row0 = t * BN;
       const float bound = fmaxf(gthr, thr_s);
+      bool released = false;  // this warp has arrived on acc_empty for this tile
       // Slow path for one 32-row chunk, kept compact (instruction-cache
       // friendly): the lane's candidate rows as a bit mask, then a small loop
       // over the set bits only, each score picked from registers.
@@ -545,8 +547,20 @@ __global__ void __launch_bounds__(THREADS, 1)
         static_assert(PART_CHUNKS == 2, "64-column part");
         float v[64];
         tmem_ld64(tmem + ((quarter * 32u) << 16) + a * BN + chalf * 64, v);
-        if (l2) {  // internal score 2 q.x - |x|^2 (same row norms for every lane: broadcast loads)
-          const float* nr = norms + row0 + chalf * 64;
+        // The part's scores are in registers: hand the accumulator back to
+        // the MMA warp now, so the next-but-one tile's MMAs overlap this
+        // warp's selection work.
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(acc_empty + a);
+        released = true;
+        // L2: the internal score is 2 q.x - |x|^2. Publish-only tiles need
+        // exact scores of real rows; the other tiles test the bound against
+        // 2 max(q.x) - (least |x|^2 of the 32-row chunk), an upper bound of
+        // the chunk's best score, and convert a chunk exactly only when that
+        // passes (rare), so the common path matches the inner product's.
+        const float* nr = norms + row0 + chalf * 64;
+        if (l2 && publish_only) {
 #pragma unroll
           for (int j = 0; j < 64; ++j) v[j] = 2.f * v[j] - __ldg(nr + j);
         }
@@ -562,10 +576,28 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (publish_only) {
           if (valid_q) { take_top(t[0]); take_top(t[16]); }
         } else {
-          const bool want0 = valid_q && t[0] >= bound;
-          if (__any_sync(0xFFFFFFFFu, want0)) slow(v, row0 + chalf * 64, 0xFFFFFFFFu, bound, want0);
-          const bool want1 = valid_q && t[16] >= bound;
-          if (__any_sync(0xFFFFFFFFu, want1)) slow(v + 32, row0 + chalf * 64 + 32, 0xFFFFFFFFu, bound, want1);
+          float u0 = t[0], u1 = t[16];
+          if (l2) {
+            const uint32_t ch = (row0 >> 5) + chalf * 2;
+            u0 = 2.f * u0 - __ldg(p.chunk_min + ch);
+            u1 = 2.f * u1 - __ldg(p.chunk_min + ch + 1);
+          }
+          const bool want0 = valid_q && u0 >= bound;
+          if (__any_sync(0xFFFFFFFFu, want0)) {
+            if (l2) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = 2.f * v[j] - __ldg(nr + j);
+            }
+            slow(v, row0 + chalf * 64, 0xFFFFFFFFu, bound, want0);
+          }
+          const bool want1 = valid_q && u1 >= bound;
+          if (__any_sync(0xFFFFFFFFu, want1)) {
+            if (l2) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[32 + j] = 2.f * v[32 + j] - __ldg(nr + 32 + j);
+            }
+            slow(v + 32, row0 + chalf * 64 + 32, 0xFFFFFFFFu, bound, want1);
+          }
         }
       } else {
 #pragma unroll 1
@@ -578,11 +610,15 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (m == 0) continue;
           float v[32];
           tmem_ld32(tmem + ((quarter * 32u) << 16) + a * BN + c * 32, v);
-          if (l2) {
+          // L2 as in the whole-part path: exact scores for publish-only
+          // tiles, else the chunk's upper bound first and exact scores only
+          // when it reaches the bound. Rows past the mask (and n_rows) are
+          // never read.
+          auto to_l2 = [&]() {
 #pragma unroll
-            for (int j = 0; j < 32; ++j)  // rows past the mask (and n_rows) are never read
-              v[j] = ((m >> j) & 1u) ? 2.f * v[j] - __ldg(norms + r0 + j) : -INFINITY;
-          }
+            for (int j = 0; j < 32; ++j) v[j] = ((m >> j) & 1u) ? 2.f * v[j] - __ldg(norms + r0 + j) : -INFINITY;
+          };
+          if (l2 && publish_only) to_l2();
           // Fast path: the best passing score of the chunk against the bound
           // (a 5-level max tree, not a 32-long dependency chain).
           float t16[16];
@@ -602,15 +638,21 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (publish_only) {
             if (valid_q) take_top(mx);
           } else {
-            const bool want = valid_q && mx >= bound;
-            if (__any_sync(0xFFFFFFFFu, want) && p.debug != 2) slow(v, r0, m, bound, want);
+            const float u = l2 ? 2.f * mx - __ldg(p.chunk_min + (r0 >> 5)) : mx;
+            const bool want = valid_q && u >= bound;
+            if (__any_sync(0xFFFFFFFFu, want) && p.debug != 2) {
+              if (l2) to_l2();
+              slow(v, r0, m, bound, want);
+            }
           }
           if (!APPEND) flush(32);  // at most 31 + 32 entries are ever buffered
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(acc_empty + a);
+      if (!released) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(acc_empty + a);
+      }
       if (APPEND && p.prologue_only && it + 1 == D && valid_q) {
         const size_t base = size_t(my_list) * 3 * p.n_queries + qi;
         p.pub_top[base] = top1 == -INFINITY ? 0u : score_key(top1);
@@ -735,6 +777,24 @@ __global__ void __launch_bounds__(128) k_spec(const uint32_t* pub_top, uint32_t 
     if (__reduce_add_sync(0xFFFFFFFFu, n) >= j) x = c;
   }
   if (lane == 0) spec_used[q] = x;
+}
+
+// L2 only: out[c] = the least squared norm of searched rows [32c, 32c + 32)
+// (the plan's rows: the shard's, or the compacted ones), the per-chunk term
+// of the epilogue's upper bound 2 max(q.x) - min |x|^2.
+__global__ void __launch_bounds__(256) k_chunk_min_norms(const SearchPlan* plan, const float* norms,
+                                                         const float* comp_norms, float* out)
+{
+  const SearchPlan pl = *plan;
+  const float* src = pl.dense ? norms : comp_norms;
+  const uint32_t n = pl.n_rows, n_chunks = (n + 31) / 32;
+  const uint32_t stride = gridDim.x * blockDim.x;
+  for (uint32_t c = blockIdx.x * blockDim.x + threadIdx.x; c < n_chunks; c += stride) {
+    const uint32_t r1 = min(n, 32 * c + 32);
+    float m = INFINITY;
+    for (uint32_t r = 32 * c; r < r1; ++r) m = fminf(m, __ldg(src + r));
+    out[c] = m;
+  }
 }
 
 // ------------------------------------------------------------------ merge
@@ -1375,7 +1435,10 @@ __global__ void __launch_bounds__(1024) k_redo_gate(const uint32_t* guard, uint3
   for (uint64_t i = threadIdx.x; i < zero_words; i += blockDim.x) zero[i] = 0u;
   __syncthreads();
   if (threadIdx.x == 0) {
-    k_topk<false><<<grid, THREADS, SMEM_TOTAL, cudaStreamTailLaunch>>>(tq, tdb, tcomp, tp);
+    if (tp.metric == CR_METRIC_L2)
+      k_topk<false, true><<<grid, THREADS, SMEM_TOTAL, cudaStreamTailLaunch>>>(tq, tdb, tcomp, tp);
+    else
+      k_topk<false, false><<<grid, THREADS, SMEM_TOTAL, cudaStreamTailLaunch>>>(tq, tdb, tcomp, tp);
     const uint64_t stride = uint64_t(tp.n_queries) * tp.k;
     k_merge<<<tp.n_queries, MERGE_THREADS, MERGE_N * 12, cudaStreamTailLaunch>>>(
         tp.part_s, tp.part_id, n_lists, tp.n_queries, tp.k, tp.metric, 0, queries, DIM, out_d, out_id, nullptr, 0,
@@ -1546,6 +1609,7 @@ struct SearchInput {
   const float* comp_norms;
   const uint32_t* idx;     // compacted row -> shard row
   const SearchPlan* plan;
+  const float* chunk_min;  // L2: least norm per 32 searched rows
 };
 
 // One search over the planned rows plus the per-query merge, stream-ordered.
@@ -1558,8 +1622,13 @@ static void run_search(const SearchInput& in, const uint16_t* d_queries, uint32_
                        bool allow_append, bool allow_spec, const uint32_t* guard, uint32_t* err,
                        bool* used_append)
 {
-  set_max_dynamic_smem(reinterpret_cast<const void*>(k_topk<true>), int(SMEM_TOTAL));
-  set_max_dynamic_smem(reinterpret_cast<const void*>(k_topk<false>), int(SMEM_TOTAL));
+  set_max_dynamic_smem(reinterpret_cast<const void*>(k_topk<true, false>), int(SMEM_TOTAL));
+  set_max_dynamic_smem(reinterpret_cast<const void*>(k_topk<false, false>), int(SMEM_TOTAL));
+  set_max_dynamic_smem(reinterpret_cast<const void*>(k_topk<true, true>), int(SMEM_TOTAL));
+  set_max_dynamic_smem(reinterpret_cast<const void*>(k_topk<false, true>), int(SMEM_TOTAL));
+  const bool l2m = metric == CR_METRIC_L2;
+  auto* const k_app = l2m ? k_topk<true, true> : k_topk<true, false>;
+  auto* const k_exact = l2m ? k_topk<false, true> : k_topk<false, false>;
   // Grid: query tiles x slices, sized for the largest plan (every shard row).
   const uint32_t max_tiles = std::max<uint32_t>(1u, div_up(in.shard_rows, BN));
   const uint32_t qtiles = div_up(n_queries, BM);
@@ -1602,6 +1671,7 @@ static void run_search(const SearchInput& in, const uint16_t* d_queries, uint32_
   tp.pass = in.pass;
   tp.norms = in.norms;
   tp.comp_norms = in.comp_norms;
+  tp.chunk_min = in.chunk_min;
   tp.row_map = in.idx;
   tp.guard = guard;
   tp.spec_capable = spec_capable ? 1u : 0u;
@@ -1645,12 +1715,12 @@ static void run_search(const SearchInput& in, const uint16_t* d_queries, uint32_
       // plan has no speculative bound).
       TopkParams pro = tp;
       pro.prologue_only = 1;
-      k_topk<true><<<grid, THREADS, SMEM_TOTAL, s>>>(tq, tdb, tcomp, pro);
+      k_app<<<grid, THREADS, SMEM_TOTAL, s>>>(tq, tdb, tcomp, pro);
       k_spec<<<div_up(n_queries, 4u), 128, 0, s>>>(tp.pub_top, 3 * n_lists, n_queries, in.plan, spec_used);
     }
     Trace::get().mark("prologue_spec", s);
-    if (append) k_topk<true><<<grid, THREADS, SMEM_TOTAL, s>>>(tq, tdb, tcomp, tp);
-    else k_topk<false><<<grid, THREADS, SMEM_TOTAL, s>>>(tq, tdb, tcomp, tp);
+    if (append) k_app<<<grid, THREADS, SMEM_TOTAL, s>>>(tq, tdb, tcomp, tp);
+    else k_exact<<<grid, THREADS, SMEM_TOTAL, s>>>(tq, tdb, tcomp, tp);
   }
   CR_CUDA(cudaGetLastError());
   if (append)
@@ -1774,6 +1844,13 @@ void filtered_topk_enqueue(const uint16_t* d_db, const float* d_db_norms, uint64
     in.comp_cap = cap_rows;
     in.comp_norms = comp_norms;
     in.idx = idx;
+  }
+  if (l2) {  // per-chunk least norms of the planned rows (the epilogue's L2 bound)
+    const uint64_t chunks = (n_rows + 31) / 32;
+    float* cm = arena.take<float>(chunks * 4 + 16);
+    k_chunk_min_norms<<<std::max<uint32_t>(1u, std::min<uint32_t>(div_up(chunks, 256), 4 * sm_count())), 256, 0,
+                        s>>>(plan, norms, in.comp_norms, cm);
+    in.chunk_min = cm;
   }
   CR_CUDA(cudaGetLastError());
   bool appended = false, unused = false;
