@@ -122,7 +122,7 @@ PortableImage parse_portable(const void* data, uint64_t n_bytes, uint32_t univer
 // Roaring image of a flat device bitset (upload.cu): canonical container
 // types under `thr`, complement above half density, bits >= U ignored.
 void upload_device_bitset(const uint32_t* d_words, uint64_t n_words, uint32_t U, uint32_t thr,
-                          cudaStream_t s, cr_gpu_roaring* out);
+                          cudaStream_t s, cr_gpu_roaring* out, bool keep_uncomplemented = false);
 uint64_t l2_bytes(int device);
 uint32_t resolve_auto(uint32_t U, int device);
 

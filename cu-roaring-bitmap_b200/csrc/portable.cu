@@ -176,11 +176,11 @@ PortableImage parse_portable(const void* data, uint64_t n_bytes, uint32_t univer
 
 using namespace crb;
 
-extern "C" int cr_upload_portable(const void* data, uint64_t n_bytes, uint32_t universe_size, cr_stream_t stream,
-                                  uint32_t bitmap_threshold, cr_gpu_roaring* out)
+static void upload_portable(const void* data, uint64_t n_bytes, uint32_t universe_size, cr_stream_t stream,
+                            uint32_t bitmap_threshold, uint32_t flags, cr_gpu_roaring* out)
 {
-  CR_API_BEGIN
   CR_REQUIRE(out != nullptr, "cr_upload_portable: null output");
+  CR_REQUIRE((flags & ~uint32_t(CR_PORTABLE_KEEP_UNCOMPLEMENTED)) == 0, "cr_upload_portable_ex: unknown flag");
   const PortableImage im = parse_portable(data, n_bytes, universe_size, "cr_upload_portable");
   const std::vector<PortableContainer>& cs = im.cs;
   const uint32_t n = uint32_t(cs.size());
@@ -206,6 +206,50 @@ extern "C" int cr_upload_portable(const void* data, uint64_t n_bytes, uint32_t u
   if (h_err & kErrBadRun) fail(CR_ERR_INVALID, "cr_upload_portable: a run passes the end of its container");
   if (h_err & kErrCardinality)
     fail(CR_ERR_INVALID, "cr_upload_portable: a container's members do not match its declared cardinality");
-  upload_device_bitset(bits.as<uint32_t>(), n_words, universe_size, bitmap_threshold, s, out);
+  upload_device_bitset(bits.as<uint32_t>(), n_words, universe_size, bitmap_threshold, s, out,
+                       (flags & CR_PORTABLE_KEEP_UNCOMPLEMENTED) != 0);
+}
+
+extern "C" int cr_upload_portable(const void* data, uint64_t n_bytes, uint32_t universe_size, cr_stream_t stream,
+                                  uint32_t bitmap_threshold, cr_gpu_roaring* out)
+{
+  CR_API_BEGIN
+  upload_portable(data, n_bytes, universe_size, stream, bitmap_threshold, 0u, out);
+  CR_API_END
+}
+
+extern "C" int cr_upload_portable_ex(const void* data, uint64_t n_bytes, uint32_t universe_size, cr_stream_t stream,
+                                     uint32_t bitmap_threshold, uint32_t flags, cr_gpu_roaring* out)
+{
+  CR_API_BEGIN
+  upload_portable(data, n_bytes, universe_size, stream, bitmap_threshold, flags, out);
+  CR_API_END
+}
+
+extern "C" int cr_portable_meta(const void* data, uint64_t n_bytes, cr_roaring_meta* out)
+{
+  CR_API_BEGIN
+  CR_REQUIRE(out != nullptr, "cr_portable_meta: null output");
+  std::memset(out, 0, sizeof(*out));
+  const PortableImage im = parse_portable(data, n_bytes, 0, "cr_portable_meta");
+  uint64_t array_elems = 0, run_pairs = 0, card = 0;
+  for (const PortableContainer& c : im.cs) {
+    if (c.kind == kKindBitmap) ++out->n_bitmap_containers;
+    else if (c.kind == kKindArray) { ++out->n_array_containers; array_elems += c.count; }
+    else { ++out->n_run_containers; run_pairs += c.count; }
+    card += c.card;
+  }
+  out->n_containers = uint32_t(im.cs.size());
+  out->total_cardinality = card;
+  if (!im.cs.empty()) {
+    const uint64_t mk = im.cs.back().key;
+    out->max_key = uint32_t(mk);
+    out->universe_size = uint32_t((mk + 1) << 16);  // the reference's u32 arithmetic: 0 for key 65535
+  }
+  // Device bytes of the containers as the reference counts them
+  // (src/upload.cpp:60-68): per container key u16, type u8, offset u32 and
+  // cardinality u16; 8 KiB per BITMAP; 2 B per ARRAY member; 4 B per run.
+  out->total_bytes = uint64_t(out->n_containers) * (2 + 1 + 4 + 2) + uint64_t(out->n_bitmap_containers) * 8192 +
+                     array_elems * 2 + run_pairs * 4;
   CR_API_END
 }

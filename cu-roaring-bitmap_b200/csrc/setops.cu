@@ -601,7 +601,31 @@ static void multi(const cr_gpu_roaring* bms, uint32_t count, bool is_or, cudaStr
   std::memset(out, 0, sizeof(*out));
   if (count == 0) return;
   CR_REQUIRE(bms != nullptr, "multi_and/multi_or: null input array");
-  CR_REQUIRE(count <= 64, "multi_and/multi_or: at most 64 inputs");
+  if (count > uint32_t(kMaxOperands)) {
+    // More inputs than one k-way pass takes: the first 64 in one pass, then
+    // the running result with the next 63 per pass (any count, like the
+    // reference's chained path, src/set_ops.cu:1733-1762).
+    cr_gpu_roaring acc{};
+    multi(bms, uint32_t(kMaxOperands), is_or, s, &acc);
+    std::vector<cr_gpu_roaring> grp;
+    for (uint32_t i = uint32_t(kMaxOperands); i < count;) {
+      const uint32_t n = std::min<uint32_t>(kMaxOperands - 1, count - i);
+      grp.assign(1, acc);
+      grp.insert(grp.end(), bms + i, bms + i + n);
+      cr_gpu_roaring next{};
+      try {
+        multi(grp.data(), n + 1, is_or, s, &next);
+      } catch (...) {
+        if (acc._alloc_base) dev_free(acc._alloc_base, s);
+        throw;
+      }
+      if (acc._alloc_base) dev_free(acc._alloc_base, s);
+      acc = next;
+      i += n;
+    }
+    *out = acc;
+    return;
+  }
   std::vector<const cr_gpu_roaring*> pos, negs;
   for (uint32_t i = 0; i < count; ++i) (bms[i].negated ? negs : pos).push_back(&bms[i]);
   // multi_and: AND(pos) minus OR(stored negs); all negated -> ~OR(stored).

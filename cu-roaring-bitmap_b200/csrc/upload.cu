@@ -38,6 +38,7 @@ struct ChunkSrc {
   const uint16_t* slot_keys; // null: slot == key (dense)
   const uint32_t* n_slots;   // device count of used slots (sparse only)
   uint32_t universe;
+  uint32_t keep_uncomplemented;  // 1: never store the complement (the reference's CRoaring upload without a universe)
 };
 
 struct PlanTotals {
@@ -153,9 +154,9 @@ __global__ void __launch_bounds__(kEmitThreads) k_analyze(ChunkSrc src, uint32_t
   }
 }
 
-__device__ __forceinline__ bool plan_negate(const unsigned long long* total, uint32_t U)
+__device__ __forceinline__ bool plan_negate(const unsigned long long* total, const ChunkSrc& src)
 {
-  return *total > static_cast<unsigned long long>(U / 2u);
+  return !src.keep_uncomplemented && *total > static_cast<unsigned long long>(src.universe / 2u);
 }
 
 // Per tile of 1024 chunk slots: totals under the two candidate thresholds.
@@ -167,7 +168,7 @@ __global__ void __launch_bounds__(kPlanTile) k_plan_tiles(ChunkSrc src, uint32_t
 {
   __shared__ unsigned long long s_red[kPlanTile / 32];
   const uint32_t i = blockIdx.x * kPlanTile + threadIdx.x;
-  const bool neg = plan_negate(total, src.universe);
+  const bool neg = plan_negate(total, src);
   uint32_t c = 0, r = 0;
   if (i < slot_count(src, max_slots)) {
     const uint4 st = stats[i];
@@ -234,7 +235,7 @@ __global__ void __launch_bounds__(kPlanTile) k_plan_emit(ChunkSrc src, uint32_t 
   __syncthreads();
   const int o = s_opt;
   const uint32_t t = o ? t1 : t0;
-  const bool neg = plan_negate(total, src.universe);
+  const bool neg = plan_negate(total, src);
   const uint32_t i = blockIdx.x * kPlanTile + threadIdx.x;
   uint32_t c = 0, r = 0;
   if (i < slot_count(src, max_slots)) {
@@ -588,7 +589,7 @@ void upload_device_ids(const uint32_t* d_ids, uint64_t n, uint32_t U, uint32_t t
 }
 
 void upload_device_bitset(const uint32_t* d_words, uint64_t n_words, uint32_t U, uint32_t thr,
-                          cudaStream_t s, cr_gpu_roaring* out)
+                          cudaStream_t s, cr_gpu_roaring* out, bool keep_uncomplemented)
 {
   std::memset(out, 0, sizeof(*out));
   out->universe_size = U;
@@ -598,6 +599,7 @@ void upload_device_bitset(const uint32_t* d_words, uint64_t n_words, uint32_t U,
   src.words = d_words;
   src.n_words = std::min<uint64_t>(n_words, uint64_t(n_chunks_for(U)) * kChunkWords32);
   src.universe = U;
+  src.keep_uncomplemented = keep_uncomplemented ? 1u : 0u;
   build_from_chunks(src, n_chunks_for(U), U, thr, nullptr, s, out);
 }
 

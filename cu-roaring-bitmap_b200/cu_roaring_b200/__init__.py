@@ -38,7 +38,7 @@ EXPORTED_SYMBOLS = (
     "cr_row_norms", "cr_topk_merge", "cr_topk_merge_packed", "cr_upload_portable", "cr_batch_upload_portable", "cr_batch_free",
     "cr_batch_promote", "cr_batch_multi_and", "cr_batch_decompress", "cr_batch_contains", "cr_filtered_topk_check", "cr_profile_enable", "cr_profile_last_ms", "cr_profile_sum_ms",
     "cr_topk_comm_unique_id", "cr_topk_comm_init", "cr_topk_comm_size", "cr_topk_comm_destroy",
-    "cr_filtered_topk_sharded",
+    "cr_filtered_topk_sharded", "cr_upload_portable_ex", "cr_portable_meta",
 )
 
 
@@ -99,6 +99,8 @@ _sigs = {
     "cr_batch_contains": ([C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint64, C.c_void_p, C.c_void_p], _i32),
     "cr_filtered_topk_check": ([], _i32),
     "cr_profile_sum_ms": ([_i32, C.POINTER(C.c_float), C.POINTER(C.c_uint32)], _i32),
+    "cr_upload_portable_ex": ([_vp, _u64, _u32, _vp, _u32, _u32, _P], _i32),
+    "cr_portable_meta": ([_vp, _u64, _vp], _i32),
     "cr_topk_comm_unique_id": ([_vp, _u32], _i32),
     "cr_topk_comm_init": ([_vp, _i32, _i32, C.POINTER(_vp)], _i32),
     "cr_topk_comm_size": ([_vp, C.POINTER(_i32), C.POINTER(_i32)], _i32),
@@ -257,13 +259,36 @@ def upload_from_device_bitset(words, universe_size: int, stream=None,
     return out
 
 
-def upload_portable(data: bytes, universe_size: int, stream=None, bitmap_threshold: int = PROMOTE_AUTO) -> GpuRoaring:
-    """A bitmap in the portable Roaring serialization (bytes) -> GpuRoaring."""
+PORTABLE_KEEP_UNCOMPLEMENTED = 1
+
+
+def upload_portable(data: bytes, universe_size: int, stream=None, bitmap_threshold: int = PROMOTE_AUTO,
+                    flags: int = 0) -> GpuRoaring:
+    """A bitmap in the portable Roaring serialization (bytes) -> GpuRoaring.
+    flags=PORTABLE_KEEP_UNCOMPLEMENTED never stores the complement."""
     out = GpuRoaring()
     buf = C.create_string_buffer(bytes(data), len(data)) if len(data) else None
-    _check(_lib.cr_upload_portable(C.cast(buf, C.c_void_p) if buf is not None else None, len(data), universe_size,
-                                   _stream_ptr(stream), bitmap_threshold, C.byref(out.raw)), "upload_portable")
+    _check(_lib.cr_upload_portable_ex(C.cast(buf, C.c_void_p) if buf is not None else None, len(data),
+                                      universe_size, _stream_ptr(stream), bitmap_threshold, flags,
+                                      C.byref(out.raw)), "upload_portable")
     return out
+
+
+class CrRoaringMeta(C.Structure):
+    _fields_ = [("n_containers", C.c_uint32), ("n_bitmap_containers", C.c_uint32),
+                ("n_array_containers", C.c_uint32), ("n_run_containers", C.c_uint32),
+                ("universe_size", C.c_uint32), ("max_key", C.c_uint32), ("total_bytes", C.c_uint64),
+                ("total_cardinality", C.c_uint64)]
+
+
+def portable_meta(data: bytes) -> dict:
+    """Container counts and device footprint of a portable serialization
+    (host only; the reference's get_meta(const roaring_bitmap_t*))."""
+    m = CrRoaringMeta()
+    buf = C.create_string_buffer(bytes(data), len(data)) if len(data) else None
+    _check(_lib.cr_portable_meta(C.cast(buf, C.c_void_p) if buf is not None else None, len(data), C.byref(m)),
+           "portable_meta")
+    return {f: getattr(m, f) for f, _ in CrRoaringMeta._fields_}
 
 
 class CrRoaringBatch(C.Structure):

@@ -106,6 +106,27 @@ int cr_upload_from_device_ids(const uint32_t* d_ids, uint64_t n_ids, uint32_t un
 int cr_upload_portable(const void* data, uint64_t n_bytes, uint32_t universe_size, cr_stream_t stream,
                        uint32_t bitmap_threshold, cr_gpu_roaring* out);
 
+/* cr_upload_portable with flags. CR_PORTABLE_KEEP_UNCOMPLEMENTED: never
+ * store the complement, whatever the density (the reference's
+ * upload(const roaring_bitmap_t*, stream, threshold) without a universe
+ * never complements, src/upload.cpp:290-294). */
+#define CR_PORTABLE_KEEP_UNCOMPLEMENTED 1u
+int cr_upload_portable_ex(const void* data, uint64_t n_bytes, uint32_t universe_size, cr_stream_t stream,
+                          uint32_t bitmap_threshold, uint32_t flags, cr_gpu_roaring* out);
+
+/* Container counts and device footprint of a portable serialization, read
+ * from its header on the host (no device work): replaces
+ * get_meta(const roaring_bitmap_t*) (reference src/upload.cpp:31-71), whose
+ * fields it fills the same way (universe_size = (max key + 1) << 16 in u32
+ * arithmetic; total_bytes = 9 B per container + 8 KiB per BITMAP + 2 B per
+ * ARRAY member + 4 B per run). */
+typedef struct cr_roaring_meta {
+  uint32_t n_containers, n_bitmap_containers, n_array_containers, n_run_containers;
+  uint32_t universe_size, max_key;
+  uint64_t total_bytes, total_cardinality;
+} cr_roaring_meta;
+int cr_portable_meta(const void* data, uint64_t n_bytes, cr_roaring_meta* out);
+
 /* Replace upload_from_bitset / upload_from_device_bitset (reference
  * src/upload_ids.cu:806-893, include/cu_roaring/detail/upload_ids.cuh:48-56).
  * Bit i is (words[i/32] >> (i%32)) & 1. Bits >= universe_size are ignored.
@@ -140,7 +161,8 @@ int cr_deep_copy(const cr_gpu_roaring* bm, cr_stream_t stream, cr_gpu_roaring* o
 int cr_set_operation(const cr_gpu_roaring* a, const cr_gpu_roaring* b, int op,
                      cr_stream_t stream, cr_gpu_roaring* out);
 /* Replace multi_and / multi_or (reference src/set_ops.cu:1715-1762).
- * count <= 64. */
+ * Any count: more than 64 inputs are combined 64 per pass (the first pass,
+ * then the running result with the next 63). */
 int cr_multi_and(const cr_gpu_roaring* bitmaps, uint32_t count, cr_stream_t stream,
                  cr_gpu_roaring* out);
 int cr_multi_or(const cr_gpu_roaring* bitmaps, uint32_t count, cr_stream_t stream,

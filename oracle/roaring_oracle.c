@@ -436,10 +436,35 @@ int or_set_operation(const or_image* a, const or_image* b, int op, or_image* out
  * :1489-1710): AND of the non-negated inputs minus the stored sets of the
  * negated ones; with no non-negated input the result is the complement of
  * the OR of the stored sets (stored negated). */
+/* More than OR_MAX_PASS inputs: the engine combines the first 64 in one
+ * k-way pass, then the running result with the next 63 per pass (its
+ * structural output typing then applies per pass); this restates that. */
+#define OR_MAX_PASS 64u
+static int multi_chained(const or_image* const* ims, uint32_t count, or_image* out,
+                         int (*one)(const or_image* const*, uint32_t, or_image*))
+{
+  or_image acc;
+  one(ims, OR_MAX_PASS, &acc);
+  const or_image* grp[OR_MAX_PASS];
+  for (uint32_t i = OR_MAX_PASS; i < count;) {
+    uint32_t n = count - i < OR_MAX_PASS - 1 ? count - i : OR_MAX_PASS - 1;
+    grp[0] = &acc;
+    for (uint32_t j = 0; j < n; ++j) grp[1 + j] = ims[i + j];
+    or_image next;
+    one(grp, n + 1, &next);
+    or_image_free(&acc);
+    acc = next;
+    i += n;
+  }
+  *out = acc;
+  return 0;
+}
+
 int or_multi_and(const or_image* const* ims, uint32_t count, or_image* out)
 {
   memset(out, 0, sizeof(*out));
   if (count == 0) return 0;
+  if (count > OR_MAX_PASS) return multi_chained(ims, count, out, or_multi_and);
   const or_image** P = (const or_image**)malloc(sizeof(void*) * count);
   const or_image** N = (const or_image**)malloc(sizeof(void*) * count);
   uint32_t np = 0, nn = 0, U = 0;
@@ -458,6 +483,7 @@ int or_multi_or(const or_image* const* ims, uint32_t count, or_image* out)
 {
   memset(out, 0, sizeof(*out));
   if (count == 0) return 0;
+  if (count > OR_MAX_PASS) return multi_chained(ims, count, out, or_multi_or);
   const or_image** P = (const or_image**)malloc(sizeof(void*) * count);
   const or_image** N = (const or_image**)malloc(sizeof(void*) * count);
   uint32_t np = 0, nn = 0, U = 0;

@@ -67,3 +67,46 @@ def test_error_path_without_gpu(built_lib):
     rc = cr.lib().cr_set_operation(None, None, 0, None, None)
     assert rc == -1
     assert b"null" in cr.lib().cr_last_error_string()
+
+
+def _layout_program(tmp_path, include_dir: Path, tag: str) -> str:
+    """Compiles and runs a host program printing sizeof / offsetof of every
+    field of GpuRoaring, GpuRoaringMeta and GpuRoaringView as declared by the
+    headers under include_dir."""
+    roaring = ["keys", "types", "offsets", "cardinalities", "n_containers", "universe_size", "total_cardinality",
+               "bitmap_data", "n_bitmap_containers", "array_data", "n_array_containers", "array_pool_bytes",
+               "run_data", "n_run_containers", "run_pool_bytes", "key_index", "max_key", "negated", "_alloc_base"]
+    meta = ["n_containers", "n_bitmap_containers", "n_array_containers", "n_run_containers", "universe_size",
+            "total_bytes"]
+    view = ["keys", "types", "offsets", "cardinalities", "n_containers", "bitmap_data", "array_data", "run_data",
+            "key_index", "max_key", "all_bitmap", "negated"]
+    lines = []
+    for struct, fields in (("GpuRoaring", roaring), ("GpuRoaringMeta", meta), ("GpuRoaringView", view)):
+        lines.append(f'  printf("{struct} size %zu\\n", sizeof(cu_roaring::{struct}));')
+        for f in fields:
+            lines.append(f'  printf("{struct}.{f} %zu\\n", offsetof(cu_roaring::{struct}, {f}));')
+    src = tmp_path / f"layout_{tag}.cu"
+    src.write_text("#include <cstddef>\n#include <cstdio>\n#include \"cu_roaring/types.cuh\"\n"
+                   "#include \"cu_roaring/device/roaring_view.cuh\"\nint main() {\n" + "\n".join(lines) +
+                   "\n  return 0;\n}\n")
+    exe = tmp_path / f"layout_{tag}"
+    subprocess.run(["/usr/local/cuda/bin/nvcc", "-std=c++17", f"-I{include_dir}", str(src), "-o", str(exe)],
+                   check=True, capture_output=True)
+    return subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout
+
+
+def test_layouts_match_the_reference_headers(tmp_path):
+    """The public structs (GpuRoaring, GpuRoaringMeta, GpuRoaringView) have the
+    reference's exact layout: the reference's own include/cu_roaring headers
+    and this engine's, compiled side by side. Runs where the reference
+    checkout is present (CU_ROARING_REFERENCE, default /root/reference)."""
+    import os
+
+    ref = Path(os.environ.get("CU_ROARING_REFERENCE", "/root/reference")) / "include"
+    if not (ref / "cu_roaring" / "types.cuh").exists():
+        import pytest
+
+        pytest.skip("reference headers not present")
+    ours = _layout_program(tmp_path, REPO / "include", "ours")
+    theirs = _layout_program(tmp_path, ref, "ref")
+    assert ours == theirs

@@ -312,3 +312,31 @@ def test_cpp_dropin_program(built_lib, cr):
     res = subprocess.run([str(exe)], capture_output=True, text=True, timeout=300)
     assert res.returncode == 0, res.stdout + res.stderr
     assert "0 failed" in res.stdout
+
+
+@pytest.mark.parametrize("count", [65, 130])
+@pytest.mark.parametrize("fn", ["and", "or"])
+def test_multi_more_than_64_inputs(cr, oracle, l2, count, fn):
+    """More inputs than one k-way pass takes (the reference accepts any
+    count, src/set_ops.cu:1733-1762): chained passes of 64, bit-exact against
+    the oracle's identical chaining and against numpy. Dense inputs (most
+    stored as complements) keep the AND non-empty; every 7th input is sparse."""
+    u = 1 << 18
+    rng = np.random.default_rng(count)
+    sets = []
+    for i in range(count):
+        p = 0.02 if i % 7 == 3 else 0.995
+        ids = np.flatnonzero(rng.random(u) < p).astype(np.uint32)
+        sets.append(truth_words(ids, u))
+    dev = [cr.upload_from_bitset(w, u) for w in sets]
+    ora = [oracle.from_bitset(w, u, AUTO, l2) for w in sets]
+    assert any(d.raw.negated for d in dev) and not all(d.raw.negated for d in dev)
+    dr = (cr.multi_and if fn == "and" else cr.multi_or)(dev)
+    orr = (oracle.multi_and if fn == "and" else oracle.multi_or)(ora)
+    assert_same_image(dr, orr, f"multi_{fn} x{count}")
+    want = sets[0].copy()
+    for w in sets[1:]:
+        want = (want & w) if fn == "and" else (want | w)
+    assert np.array_equal(cr.decompress_to_bitset(dr).cpu().numpy().view(np.uint32), want)
+    for x in dev + [dr]:
+        x.free()
