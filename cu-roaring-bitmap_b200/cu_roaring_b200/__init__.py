@@ -38,7 +38,8 @@ EXPORTED_SYMBOLS = (
     "cr_row_norms", "cr_topk_merge", "cr_topk_merge_packed", "cr_upload_portable", "cr_batch_upload_portable", "cr_batch_free",
     "cr_batch_promote", "cr_batch_multi_and", "cr_batch_decompress", "cr_batch_contains", "cr_filtered_topk_check", "cr_profile_enable", "cr_profile_last_ms", "cr_profile_sum_ms",
     "cr_topk_comm_unique_id", "cr_topk_comm_init", "cr_topk_comm_size", "cr_topk_comm_destroy",
-    "cr_filtered_topk_sharded", "cr_upload_portable_ex", "cr_portable_meta",
+    "cr_filtered_topk_sharded", "cr_upload_portable_ex", "cr_portable_meta", "cr_key_range", "cr_key_slice",
+    "cr_concat_key_slices",
 )
 
 
@@ -99,6 +100,9 @@ _sigs = {
     "cr_batch_contains": ([C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint64, C.c_void_p, C.c_void_p], _i32),
     "cr_filtered_topk_check": ([], _i32),
     "cr_profile_sum_ms": ([_i32, C.POINTER(C.c_float), C.POINTER(C.c_uint32)], _i32),
+    "cr_key_range": ([_u32, _u32, _u32, C.POINTER(_u32), C.POINTER(_u32)], _i32),
+    "cr_key_slice": ([_P, _u32, _u32, _vp, _P], _i32),
+    "cr_concat_key_slices": ([_P, _u32, _vp, _P], _i32),
     "cr_upload_portable_ex": ([_vp, _u64, _u32, _vp, _u32, _u32, _P], _i32),
     "cr_portable_meta": ([_vp, _u64, _vp], _i32),
     "cr_topk_comm_unique_id": ([_vp, _u32], _i32),
@@ -612,6 +616,29 @@ def profile_last_ms(kernel: int) -> float:
 
 
 # ------------------------------------------------------------- sharding
+
+def key_range(universe_size: int, rank: int, world: int) -> tuple[int, int]:
+    """Rank `rank`'s container keys [lo, hi) when a bitmap over universe_size
+    is split at chunk (65536-ID) boundaries over `world` ranks."""
+    lo, hi = C.c_uint32(), C.c_uint32()
+    _check(_lib.cr_key_range(universe_size, rank, world, C.byref(lo), C.byref(hi)), "key_range")
+    return lo.value, hi.value
+
+
+def key_slice(bm: GpuRoaring, key_lo: int, key_hi: int, stream=None) -> GpuRoaring:
+    """The containers of `bm` with keys in [key_lo, key_hi), as a new bitmap."""
+    out = GpuRoaring()
+    _check(_lib.cr_key_slice(C.byref(bm.raw), key_lo, key_hi, _stream_ptr(stream), C.byref(out.raw)), "key_slice")
+    return out
+
+
+def concat_key_slices(slices, stream=None) -> GpuRoaring:
+    """Slices with ascending, disjoint key ranges laid end to end."""
+    out = GpuRoaring()
+    arr = (CrGpuRoaring * max(1, len(slices)))(*[b.raw for b in slices])
+    _check(_lib.cr_concat_key_slices(arr, len(slices), _stream_ptr(stream), C.byref(out.raw)), "concat_key_slices")
+    return out
+
 
 def shard_range(n_rows: int, rank: int, world: int) -> tuple[int, int]:
     """Contiguous row range [lo, hi) of `rank` when n_rows are split over

@@ -168,6 +168,25 @@ int cr_multi_and(const cr_gpu_roaring* bitmaps, uint32_t count, cr_stream_t stre
 int cr_multi_or(const cr_gpu_roaring* bitmaps, uint32_t count, cr_stream_t stream,
                 cr_gpu_roaring* out);
 
+/* ---- Key-range sharding across GPUs (no reference counterpart: the
+ * reference has no multi-GPU path) --------------------------------------------
+ * Set operations, multi_and / multi_or and point queries work chunk by chunk
+ * (65536 IDs per key), so G ranks split every operand at chunk boundaries,
+ * rank g holding keys [g*K/G, (g+1)*K/G) with K = ceil(universe / 65536),
+ * and compute with no communication; the result slices laid end to end are
+ * the unsharded result, container for container.
+ * cr_key_range gives a rank's key range; cr_key_slice copies a bitmap's
+ * containers in [key_lo, key_hi) into a new bitmap (same universe, types and
+ * complement flag); cr_concat_key_slices lays slices with ascending,
+ * disjoint key ranges end to end (pool offsets rebased, key index rebuilt).
+ * total_cardinality of a slice or a concatenation counts as if it were the
+ * whole bitmap (U minus the stored members when the complement is stored).
+ * Both synchronise `stream` (they plan the copy on the host). */
+int cr_key_range(uint32_t universe_size, uint32_t rank, uint32_t n_ranks, uint32_t* key_lo, uint32_t* key_hi);
+int cr_key_slice(const cr_gpu_roaring* bm, uint32_t key_lo, uint32_t key_hi, cr_stream_t stream,
+                 cr_gpu_roaring* out);
+int cr_concat_key_slices(const cr_gpu_roaring* slices, uint32_t n, cr_stream_t stream, cr_gpu_roaring* out);
+
 /* ---- Export ------------------------------------------------------------------ */
 
 /* Replaces decompress_to_bitset (reference src/decompress.cu:104-162).
