@@ -1,5 +1,6 @@
 // cu_roaring B200 engine — errors, packed allocation, device queries, free,
 // deep copy, threshold resolution.
+#include <atomic>
 #include <map>
 #include <mutex>
 #include <vector>
@@ -44,10 +45,18 @@ static void keep_pool_memory()
   cudaGetLastError();
 }
 
+// Allocation-failure injection for tests (cr_test_fail_allocations): the
+// number of device allocations still allowed to succeed, -1 = no injection.
+static std::atomic<int64_t> g_allocs_left{-1};
+
 void* dev_alloc(size_t bytes, cudaStream_t s)
 {
   void* p = nullptr;
   if (bytes == 0) return nullptr;
+  for (int64_t left = g_allocs_left.load(); left >= 0;) {
+    if (left == 0) fail(CR_ERR_OOM, "cudaMallocAsync(" + std::to_string(bytes) + " bytes) failed: injected failure");
+    if (g_allocs_left.compare_exchange_weak(left, left - 1)) break;
+  }
   keep_pool_memory();
   const cudaError_t e = cudaMallocAsync(&p, bytes, s);
   if (e != cudaSuccess) {
@@ -352,4 +361,10 @@ extern "C" int cr_deep_copy(const cr_gpu_roaring* bm, cr_stream_t stream, cr_gpu
   CR_REQUIRE(bm && out, "cr_deep_copy: null argument");
   deep_copy(bm, out, reinterpret_cast<cudaStream_t>(stream));
   CR_API_END
+}
+
+extern "C" int cr_test_fail_allocations(int64_t after)
+{
+  crb::g_allocs_left.store(after < 0 ? -1 : after);
+  return CR_OK;
 }

@@ -111,6 +111,9 @@ struct TopkParams {
   uint32_t* err;
   uint32_t* shared_thr;  // [Q] order-preserving bits of the best known k-th score
   uint32_t debug;        // measurement only: 1 = skip the epilogue's score work
+                         // (7 = the producer loads nothing: every pipeline wait
+                         // runs out; failure tests only)
+  uint32_t spin_limit;   // polls per pipeline wait before it gives up (kSpinLimit)
   float* buf_s;          // per-CTA candidate buffers: [cta][EPI][BUF] (global, L2-resident)
   uint32_t* buf_r;
   uint32_t* pub;         // [Q][n_lists] published j-th best of every partial list (score keys)
@@ -322,7 +325,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (warp == 0) {
     // ---------------- TMA producer
-    if (lane == 0) {
+    if (lane == 0 && p.debug != 7) {
       prefetch_tmap(&tq);
       prefetch_tmap(tdbp);
       mbar_expect_tx(q_full, 2 * KB_BYTES_Q);
@@ -330,7 +333,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       tma_load_2d(&tq, q_full, sQ + KB_BYTES_Q, 64, int32_t(qt * BM));
       for (uint32_t it = 0; it < n_it; ++it) {
         const uint32_t t = tile_of(it), s = it % STAGES;
-        if (!mbar_wait(empty + s, ((it / STAGES) & 1u) ^ 1u, p.err, 1u)) break;
+        if (!mbar_wait(empty + s, ((it / STAGES) & 1u) ^ 1u, p.err, 1u, p.spin_limit)) break;
         uint8_t* dst = sDB + s * STAGE_BYTES;
         mbar_expect_tx(full + s, STAGE_BYTES);
         tma_load_2d(tdbp, full + s, dst, 0, int32_t(t * BN));
@@ -340,12 +343,12 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else if (warp == 1) {
     // ---------------- UMMA issuer
     if (lane == 0) {
-      bool ok = mbar_wait(q_full, 0, p.err, 2u);
+      bool ok = mbar_wait(q_full, 0, p.err, 2u, p.spin_limit);
       const uint32_t aq = smem_addr(sQ);
       for (uint32_t it = 0; it < n_it && ok; ++it) {
         const uint32_t s = it % STAGES, a = it & 1u;
-        if (!mbar_wait(full + s, (it / STAGES) & 1u, p.err, 4u)) break;
-        if (!mbar_wait(acc_empty + a, ((it >> 1) & 1u) ^ 1u, p.err, 8u)) break;
+        if (!mbar_wait(full + s, (it / STAGES) & 1u, p.err, 4u, p.spin_limit)) break;
+        if (!mbar_wait(acc_empty + a, ((it >> 1) & 1u) ^ 1u, p.err, 8u, p.spin_limit)) break;
         tc_fence_after();
         const uint32_t adb = smem_addr(sDB + s * STAGE_BYTES);
 #pragma unroll
@@ -476,7 +479,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         // n_lists * jth >= k: the minimum over lists bounds the k-th best.
         gthr = fmaxf(gthr, reinterpret_cast<volatile float*>(s_bound)[t_local]);
       }
-      if (!mbar_wait(acc_full + a, (it >> 1) & 1u, p.err, 16u)) break;
+      if (!mbar_wait(acc_full + a, (it >> 1) & 1u, p.err, 16u, p.spin_limit)) break;
       tc_fence_after();
       const uint32_t row0 = t * BN;
       const float bound = fmaxf(gthr, thr_s);
@@ -1694,6 +1697,9 @@ static void run_search(const SearchInput& in, const uint16_t* d_queries, uint32_
   tp.part_s = reinterpret_cast<float*>(p); p += part_b * 4;
   if (const char* dbg = getenv("CR_TOPK_DEBUG")) tp.debug = uint32_t(atoi(dbg));
   tp.keeper_ns = 2000;
+  tp.spin_limit = kSpinLimit;
+  // Failure tests only: a short limit for every pipeline wait.
+  if (const char* sl = getenv("CR_TOPK_SPIN_LIMIT")) tp.spin_limit = std::max(1, atoi(sl));
   if (const char* kn = getenv("CR_TOPK_KEEPER_NS")) tp.keeper_ns = uint32_t(atoi(kn));
   Trace::get().mark("setup", s);
   const CUtensorMap tq = make_map(d_queries, n_queries, BM);

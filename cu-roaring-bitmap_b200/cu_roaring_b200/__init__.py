@@ -39,7 +39,7 @@ EXPORTED_SYMBOLS = (
     "cr_batch_promote", "cr_batch_multi_and", "cr_batch_decompress", "cr_batch_contains", "cr_filtered_topk_check", "cr_profile_enable", "cr_profile_last_ms", "cr_profile_sum_ms",
     "cr_topk_comm_unique_id", "cr_topk_comm_init", "cr_topk_comm_size", "cr_topk_comm_destroy",
     "cr_filtered_topk_sharded", "cr_upload_portable_ex", "cr_portable_meta", "cr_key_range", "cr_key_slice",
-    "cr_concat_key_slices",
+    "cr_concat_key_slices", "cr_test_fail_allocations",
 )
 
 
@@ -100,6 +100,7 @@ _sigs = {
     "cr_batch_contains": ([C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint64, C.c_void_p, C.c_void_p], _i32),
     "cr_filtered_topk_check": ([], _i32),
     "cr_profile_sum_ms": ([_i32, C.POINTER(C.c_float), C.POINTER(C.c_uint32)], _i32),
+    "cr_test_fail_allocations": ([C.c_int64], _i32),
     "cr_key_range": ([_u32, _u32, _u32, C.POINTER(_u32), C.POINTER(_u32)], _i32),
     "cr_key_slice": ([_P, _u32, _u32, _vp, _P], _i32),
     "cr_concat_key_slices": ([_P, _u32, _vp, _P], _i32),

@@ -361,6 +361,13 @@ int cr_batch_decompress(const cr_roaring_batch* in, uint64_t* d_bitsets, uint64_
 int cr_batch_contains(const cr_roaring_batch* in, const uint32_t* d_bitmap_idx, const uint32_t* d_ids, uint64_t n,
                       uint32_t* d_out_bits, cr_stream_t stream);
 
+/* ---- Fault injection for tests (no reference counterpart) -------------------
+ * After `after` more successful device allocations, every later one inside
+ * the library fails as if the device were out of memory (CR_ERR_OOM);
+ * after < 0 switches injection off. Process-wide. For testing callers'
+ * error paths: no call may leak or leave a half-built bitmap behind. */
+int cr_test_fail_allocations(int64_t after);
+
 /* ---- Measurement hooks (no reference counterpart) ---------------------------
  * When enabled, the library brackets its dominant kernels with CUDA events on
  * the launching stream; cr_profile_last_ms returns the device time of the
