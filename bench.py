@@ -600,7 +600,7 @@ def c2_metrics(torch, cr, pk, fails, g, threads):
 
 # ------------------------------------------------------------ config 3
 
-def c3_bitmaps(torch, cr, g, U, dev):
+def c3_bitmaps(torch, cr, g, U, dev, host=True):
     """The eight predicates: Bernoulli 0.5 / 0.1 / 0.01 / 0.001, two clustered
     run sets at ~20% (lengths uniform in [1, 8192], gaps in [1, 32768]), two
     Zipf(1.1) ID sets (1.07e7 draws, ranks spread by an odd multiplier mod
@@ -609,7 +609,7 @@ def c3_bitmaps(torch, cr, g, U, dev):
     for p_ in (0.5, 0.1, 0.01, 0.001):
         w = bernoulli_words(torch, g, U, p_, dev)
         bms.append(cr.upload_from_device_bitset(w, U))
-        src.append(("bitset", w.cpu().numpy().view(np.uint32)))
+        src.append(("bitset", w.cpu().numpy().view(np.uint32) if host else None))
         del w
     for _ in range(2):
         ln = torch.randint(1, 8193, (70000,), device=dev, generator=g)
@@ -621,7 +621,7 @@ def c3_bitmaps(torch, cr, g, U, dev):
         pos = torch.arange(off.numel(), device=dev) - torch.repeat_interleave(torch.cumsum(ln, 0) - ln, ln)
         ids = (st[off] + pos).to(torch.int32)
         bms.append(cr.upload_from_ids(ids, U))
-        src.append(("ids", ids.cpu().numpy().view(np.uint32)))
+        src.append(("ids", ids.cpu().numpy().view(np.uint32) if host else None))
     rng = np.random.default_rng(5)
     for _ in range(2):
         z = rng.zipf(1.1, 10_700_000)
@@ -817,6 +817,70 @@ def c4_metrics(torch, cr, pk, fails, g, threads):
             "parity": "checked" if all(p == "checked" for p in par) else "FAILED"}
 
 
+def c3_sharded(torch, dist, cr, pk, fails, rank, world):
+    """Config 3's multi_and over 3 / 5 / 8 predicates with the bitmaps split
+    by container-key range over the ranks (cr_key_slice): each rank combines
+    its slices with no communication. Time = max over ranks of the API call
+    (CUDA events, 5 calls); bytes = the operand containers at keys common to
+    all inputs plus the result, summed over ranks. Rank 0 checks the ranks'
+    result IDs laid end to end against the unsharded multi_and."""
+    U = 1 << 30
+    dev = "cuda"
+    g = torch.Generator(device=dev).manual_seed(31)
+    bms, _ = c3_bitmaps(torch, cr, g, U, dev, host=False)
+    lo, hi = cr.key_range(U, rank, world)
+    sl = [cr.key_slice(b, lo, hi) for b in bms]
+    stream = torch.cuda.current_stream()
+    out = {"universe": U, "key_range_rank0": cr.key_range(U, 0, world)}
+    ok = []
+    for cnt in (3, 5, 8):
+        sel = sl[:cnt]
+        for _ in range(2):
+            cr.multi_and(sel).free()
+        dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(5):
+            cr.multi_and(sel).free()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        r = cr.multi_and(sel)
+        ims = [b.image() for b in sel]
+        keys = ims[0]["keys"]
+        for im in ims[1:]:
+            keys = np.intersect1d(keys, im["keys"], assume_unique=True)
+        algo = image_payload(r.image())
+        for im in ims:
+            m = np.isin(im["keys"], keys, assume_unique=True)
+            algo += payload_bytes(im["types"][m], im["cards"][m]) + 9 * int(m.sum())
+        t = torch.tensor([e0.elapsed_time(e1) / 5, float(algo)], device=dev, dtype=torch.float64)
+        tmax = t.clone()
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        ids = cr.enumerate_ids(r, dtype="uint32").cpu().numpy().view(np.uint32)
+        parts = [None] * world if rank == 0 else None
+        dist.gather_object(ids, parts, dst=0)
+        par = "checked"
+        if rank == 0:
+            w = cr.multi_and(bms[:cnt])
+            want = cr.enumerate_ids(w, dtype="uint32").cpu().numpy().view(np.uint32)
+            w.free()
+            par = fails.check(f"c3 sharded multi_and {cnt}", lambda: _require_equal(np.concatenate(parts), want,
+                                                                                    "sharded multi_and"))
+        ok.append(par)
+        ms = float(tmax[0].item())
+        out[str(cnt)] = {"api_ms_max_over_ranks": ms, "algorithmic_bytes_all_ranks": t[1].item(),
+                         "api_GBps_all_ranks": t[1].item() / ms / 1e6,
+                         "roofline_frac_api_per_gpu": t[1].item() / ms / 1e6 / (pk["hbm_gbs"] * world),
+                         "parity": par}
+        r.free()
+    for b in sl + bms:
+        b.free()
+    out["parity"] = "checked" if all(p == "checked" for p in ok) else "FAILED"
+    return out
+
+
 def secondary_metrics(torch, cr, pk, fails, threads):
     g = torch.Generator(device="cuda").manual_seed(11)
     out = {}
@@ -978,6 +1042,10 @@ def main():
 
     secondary = None
     cpu = None
+    which = "none" if args.no_secondary else args.secondary
+    sharded = None
+    if world > 1 and which in ("all", "roaring"):
+        sharded = c3_sharded(torch, dist, cr, pk, fails, rank, world)
     if rank == 0:
         if world == 1:
             sample_rows = min(1 << 23, n_rows)  # ~10-15 s of CPU work on the box's cores
@@ -986,7 +1054,8 @@ def main():
                                             pass_words_of(mask_np), N_QUERIES, threads)
             cpu = {"value": qps, "unit": "queries/s", "cores": threads, "kind": "port",
                    "sample": desc, "seconds": dt}
-        which = "none" if args.no_secondary else args.secondary
+        if sharded is not None:
+            secondary = {"c3_multi_and_key_sharded": sharded}
         if which != "none" and world == 1:
             secondary = {}
             if which in ("all", "topk"):
