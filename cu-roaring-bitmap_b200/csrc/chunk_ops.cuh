@@ -62,6 +62,27 @@ __device__ __forceinline__ void expand_to_smem(const DevBitmap& b, const Contain
       const uint32_t v = __ldg(a + j);
       atomicOr(reinterpret_cast<unsigned long long*>(sm + (v >> 6)), 1ull << (v & 63));
     }
+  } else if (c.idx >= 0 && c.type == kRun && c.card <= 64) {
+    // Few (typically long) runs: the whole block fills each run's words
+    // together instead of one thread walking a run word by word.
+    __shared__ uint32_t s_runs[64];
+    const uint16_t* r = b.run + (c.off >> 1);
+    if (threadIdx.x < c.card) {
+      const uint32_t s = __ldg(r + 2 * threadIdx.x);
+      s_runs[threadIdx.x] = (s << 16) | min(65535u, s + __ldg(r + 2 * threadIdx.x + 1));
+    }
+    __syncthreads();
+    for (uint32_t j = 0; j < c.card; ++j) {
+      const uint32_t s = s_runs[j] >> 16, e = s_runs[j] & 0xFFFFu;
+      const uint32_t ws = s >> 6, we = e >> 6;
+      for (uint32_t w = ws + threadIdx.x; w <= we; w += NT) {
+        uint64_t m = ~0ull;
+        if (w == ws) m &= ~0ull << (s & 63);
+        if (w == we) m &= (~0ull) >> (63 - (e & 63));
+        if (m == ~0ull) sm[w] = ~0ull;
+        else atomicOr(reinterpret_cast<unsigned long long*>(sm + w), m);
+      }
+    }
   } else if (c.idx >= 0 && c.type == kRun) {
     const uint16_t* r = b.run + (c.off >> 1);
     for (uint32_t j = threadIdx.x; j < c.card; j += NT) {

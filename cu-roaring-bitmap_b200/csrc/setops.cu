@@ -195,7 +195,9 @@ __device__ __forceinline__ void store4(uint64_t* dst, const uint64_t w[4])
 }
 
 // One CTA per work item. counts[w] = element count of the result container.
-__global__ void __launch_bounds__(256) k_execute(const Operands* __restrict__ ops_p,
+// Eight resident blocks per SM (32 registers a thread): the block's work is a
+// short chain of dependent loads, so latency hiding needs occupancy.
+__global__ void __launch_bounds__(256, 8) k_execute(const Operands* __restrict__ ops_p,
                                                  const uint4* __restrict__ work,
                                                  cr_gpu_roaring out, uint16_t* arr_scratch,
                                                  uint32_t* counts)
