@@ -1,7 +1,7 @@
 // cu_roaring B200 engine — thin inline-PTX wrappers for sm_100a:
 // mbarriers, TMA tile loads, tcgen05 (TMEM allocation, UMMA, commit, loads).
 //
-// Every mbarrier wait is bounded: after kSpinLimit polls it records an error
+// Every mbarrier wait is bounded: after kSpinLimit suspending polls it records an error
 // code in *err and returns false, so a broken pipeline ends the kernel with a
 // status the host reads instead of hanging the GPU.
 #pragma once
@@ -11,7 +11,12 @@
 namespace crb {
 namespace sm100 {
 
-constexpr uint32_t kSpinLimit = 1u << 22;
+constexpr uint32_t kSpinLimit = 1u << 16;
+// Each poll may suspend the thread in hardware for up to this long (it
+// resumes as soon as the phase completes), so waiting warps do not spin on
+// the issue slots and ALUs the working warps need; a wait gives up after
+// about kSpinLimit * kSuspendNs (1.3 s).
+constexpr uint32_t kSuspendNs = 20000;
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p)
 {
@@ -45,10 +50,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity)
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_addr(bar)), "r"(parity)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(kSuspendNs)
       : "memory");
   return ok != 0;
 }
@@ -59,7 +64,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
 {
   for (uint32_t i = 0; i < limit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (i > 64) __nanosleep(64);
   }
   atomicOr(err, code);
   return false;

@@ -110,7 +110,8 @@ struct TopkParams {
   uint64_t row_offset;
   uint32_t* err;
   uint32_t* shared_thr;  // [Q] order-preserving bits of the best known k-th score
-  uint32_t debug;        // measurement only: 1 = skip the epilogue's score work
+  uint32_t debug;        // measurement only: 1 = skip the epilogue's score work,
+                         // 8 = no database tile loads (MMAs on stale tiles), 9 = both
                          // (7 = the producer loads nothing: every pipeline wait
                          // runs out; failure tests only)
   uint32_t spin_limit;   // polls per pipeline wait before it gives up (kSpinLimit)
@@ -256,6 +257,41 @@ __device__ __forceinline__ float pick32(const float* v, uint32_t j)
   return a[0];
 }
 
+// Three-input maximum (sm_100 max.f32 with three sources): a 32-value
+// maximum in 16 instructions instead of 31.
+__device__ __forceinline__ float fmax3(float a, float b, float c)
+{
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+__device__ __forceinline__ float max8(const float* v)
+{
+  return fmax3(fmax3(v[0], v[1], v[2]), fmax3(v[3], v[4], v[5]), fmaxf(v[6], v[7]));
+}
+
+// v[j] for a run-time j < 8 (a 3-level select tree, no local memory).
+__device__ __forceinline__ float pick8(const float* v, uint32_t j)
+{
+  const float a0 = (j & 4u) ? v[4] : v[0], a1 = (j & 4u) ? v[5] : v[1], a2 = (j & 4u) ? v[6] : v[2],
+              a3 = (j & 4u) ? v[7] : v[3];
+  const float b0 = (j & 2u) ? a2 : a0, b1 = (j & 2u) ? a3 : a1;
+  return (j & 1u) ? b1 : b0;
+}
+
+__device__ __forceinline__ float max32(const float* v)
+{
+  float a[12];
+#pragma unroll
+  for (int j = 0; j < 10; ++j) a[j] = fmax3(v[3 * j], v[3 * j + 1], v[3 * j + 2]);
+  a[10] = v[30];
+  a[11] = v[31];
+  const float b0 = fmax3(a[0], a[1], a[2]), b1 = fmax3(a[3], a[4], a[5]), b2 = fmax3(a[6], a[7], a[8]),
+              b3 = fmax3(a[9], a[10], a[11]);
+  return fmaxf(fmax3(b0, b1, b2), b3);
+}
+
 template <bool APPEND, bool L2>
 __global__ void __launch_bounds__(THREADS, 1)
     k_topk(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tdb,
@@ -335,6 +371,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         const uint32_t t = tile_of(it), s = it % STAGES;
         if (!mbar_wait(empty + s, ((it / STAGES) & 1u) ^ 1u, p.err, 1u, p.spin_limit)) break;
         uint8_t* dst = sDB + s * STAGE_BYTES;
+        if (p.debug == 8 || p.debug == 9) {  // measurement only: no database loads (stale tiles)
+          mbar_arrive(full + s);
+          continue;
+        }
         mbar_expect_tx(full + s, STAGE_BYTES);
         tma_load_2d(tdbp, full + s, dst, 0, int32_t(t * BN));
         tma_load_2d(tdbp, full + s, dst + KB_BYTES_DB, 64, int32_t(t * BN));
@@ -529,6 +569,30 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
         }
       };
+      // Candidates among 8 exact scores e[] of rows r0..r0+7 (append mode):
+      // every score at or above lb is appended. With `exact_max` (gm is the
+      // exact maximum of e) a single candidate's score is gm itself.
+      auto group8 = [&](const float* e, uint32_t r0, float lb, bool exact_max, float gm) {
+        uint32_t cm = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) cm |= (e[j] >= lb ? 1u : 0u) << j;
+        const bool one = exact_max && __popc(cm) == 1;
+#pragma unroll 1
+        for (uint32_t x = cm; x; x &= x - 1) {
+          const uint32_t j = __ffs(x) - 1;
+          const float val = one ? gm : pick8(e, j);
+          if (nc < p.cap) {
+            p.cand_s[cand_base + nc] = val;
+            p.cand_r[cand_base + nc] = r0 + j;
+          }
+          ++nc;
+          if (fast_pub && it < T && val > top3) {
+            if (val > top1) { top3 = top2; top2 = top1; top1 = val; }
+            else if (val > top2) { top3 = top2; top2 = val; }
+            else { top3 = val; }
+          }
+        }
+      };
       // Publish-only tiles keep just the list's best three, fed with the
       // maximum of every 32-row chunk (real scores of distinct rows, so each
       // list still holds three rows at or above them).
@@ -541,7 +605,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       };
       // Whole-part fast path: every row of the part is searched (no mask, or
       // both of its mask words full).
-      const bool whole = APPEND && row0 + BN <= n_rows && p.debug == 0 &&
+      const bool whole = APPEND && row0 + BN <= n_rows && (p.debug == 0 || p.debug == 8 || p.debug >= 10) &&
                          (!pass || (__ldg(pass + ((row0 >> 5) + chalf * 2)) & __ldg(pass + ((row0 >> 5) + chalf * 2 + 1))) ==
                                        0xFFFFFFFFu);
       if (whole) {
@@ -567,44 +631,42 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
           for (int j = 0; j < 64; ++j) v[j] = 2.f * v[j] - __ldg(nr + j);
         }
-        // Max trees of the two 32-row halves (the slow path then runs only
-        // for a half that has a candidate in some lane).
-        float t[32];
+        // Maxima of the eight 8-row groups and of the two 32-row halves: a
+        // half is opened only when some lane's half maximum reaches the
+        // bound, and then only the groups whose maximum reaches it (usually
+        // one, holding a single candidate whose score is that maximum).
+        float g[8];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) { t[j] = fmaxf(v[j], v[j + 16]); t[16 + j] = fmaxf(v[32 + j], v[48 + j]); }
-#pragma unroll
-        for (int w = 8; w >= 1; w >>= 1)
-#pragma unroll
-          for (int j = 0; j < w; ++j) { t[j] = fmaxf(t[j], t[j + w]); t[16 + j] = fmaxf(t[16 + j], t[16 + j + w]); }
-        if (publish_only) {
-          if (valid_q) { take_top(t[0]); take_top(t[16]); }
+        for (int i = 0; i < 8; ++i) g[i] = max8(v + 8 * i);
+        const float h0 = fmaxf(fmax3(g[0], g[1], g[2]), g[3]), h1 = fmaxf(fmax3(g[4], g[5], g[6]), g[7]);
+        if (p.debug == 11) {  // measurement only: TMEM load and max trees, nothing else
+          if (h0 == 12345.f && h1 == 12345.f) p.err[3] = 1u;
+        } else if (publish_only) {
+          if (valid_q) { take_top(h0); take_top(h1); }
         } else {
-          float u0 = t[0], u1 = t[16];
-          if (l2) {
-            const uint32_t ch = (row0 >> 5) + chalf * 2;
-            u0 = 2.f * u0 - __ldg(p.chunk_min + ch);
-            u1 = 2.f * u1 - __ldg(p.chunk_min + ch + 1);
-          }
-          const bool want0 = valid_q && u0 >= bound;
-          if (__any_sync(0xFFFFFFFFu, want0)) {
-            if (l2) {
+          const uint32_t ch = (row0 >> 5) + chalf * 2;
+          const float cmin0 = l2 ? __ldg(p.chunk_min + ch) : 0.f, cmin1 = l2 ? __ldg(p.chunk_min + ch + 1) : 0.f;
 #pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] = 2.f * v[j] - __ldg(nr + j);
-            }
-            slow(v, row0 + chalf * 64, 0xFFFFFFFFu, bound, want0);
-          }
-          const bool want1 = valid_q && u1 >= bound;
-          if (__any_sync(0xFFFFFFFFu, want1)) {
-            if (l2) {
+          for (uint32_t hh = 0; hh < 2; ++hh) {
+            const float cmin = hh ? cmin1 : cmin0;
+            const float u = l2 ? 2.f * (hh ? h1 : h0) - cmin : (hh ? h1 : h0);
+            const bool want = valid_q && u >= bound && p.debug != 10;
+            if (!__any_sync(0xFFFFFFFFu, want)) continue;
 #pragma unroll
-              for (int j = 0; j < 32; ++j) v[32 + j] = 2.f * v[32 + j] - __ldg(nr + 32 + j);
+            for (uint32_t gi = 0; gi < 4; ++gi) {
+              const uint32_t gx = 4 * hh + gi;
+              const float ug = l2 ? 2.f * g[gx] - cmin : g[gx];
+              if (!(want && ug >= bound)) continue;
+              float e[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) e[j] = l2 ? 2.f * v[8 * gx + j] - __ldg(nr + 8 * gx + j) : v[8 * gx + j];
+              group8(e, row0 + chalf * 64 + 8 * gx, bound, !l2, g[gx]);
             }
-            slow(v + 32, row0 + chalf * 64 + 32, 0xFFFFFFFFu, bound, want1);
           }
         }
       } else {
 #pragma unroll 1
-        for (uint32_t c = chalf * PART_CHUNKS; c < (p.debug == 1 ? 0u : (chalf + 1) * PART_CHUNKS); ++c) {
+        for (uint32_t c = chalf * PART_CHUNKS; c < ((p.debug == 1 || p.debug == 9) ? 0u : (chalf + 1) * PART_CHUNKS); ++c) {
           const uint32_t r0 = row0 + c * 32;
           if (r0 >= n_rows) break;
           uint32_t m = pass ? __ldg(pass + (r0 >> 5)) : 0xFFFFFFFFu;
@@ -624,20 +686,15 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (l2 && publish_only) to_l2();
           // Fast path: the best passing score of the chunk against the bound
           // (a 5-level max tree, not a 32-long dependency chain).
-          float t16[16];
+          float mx;
           if (m == 0xFFFFFFFFu) {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) t16[j] = fmaxf(v[j], v[j + 16]);
+            mx = max32(v);
           } else {
+            float vm[32];
 #pragma unroll
-            for (int j = 0; j < 16; ++j)
-              t16[j] = fmaxf(((m >> j) & 1u) ? v[j] : -INFINITY, ((m >> (j + 16)) & 1u) ? v[j + 16] : -INFINITY);
+            for (int j = 0; j < 32; ++j) vm[j] = ((m >> j) & 1u) ? v[j] : -INFINITY;
+            mx = max32(vm);
           }
-#pragma unroll
-          for (int w = 8; w >= 1; w >>= 1)
-#pragma unroll
-            for (int j = 0; j < w; ++j) t16[j] = fmaxf(t16[j], t16[j + w]);
-          const float mx = t16[0];
           if (publish_only) {
             if (valid_q) take_top(mx);
           } else {
@@ -662,7 +719,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         p.pub_top[base + p.n_queries] = top2 == -INFINITY ? 0u : score_key(top2);
         p.pub_top[base + 2 * size_t(p.n_queries)] = top3 == -INFINITY ? 0u : score_key(top3);
       }
-      if (fast_pub && valid_q) {
+      if (fast_pub && valid_q && p.debug < 10) {
         const float xj = p.jth == 1 ? top1 : (p.jth == 2 ? top2 : top3);
         const uint32_t key = xj == -INFINITY ? 0u : score_key(xj);
         if (key > published) {
