@@ -895,6 +895,56 @@ def secondary_metrics(torch, cr, pk, fails, threads):
     return out
 
 
+# ------------------------------------------------------- profiling case
+
+def profile_case():
+    """`--profile-case`: every secondary kernel a few times on a reduced,
+    still larger-than-L2 case (a few GB on the device at most), for ncu
+    captures: upload of 1e8 config-2 IDs, the config-3 predicates with a
+    3-way multi_and, an all-BITMAP AND, decompress and to_csr, 2^26 point
+    queries, and a 1M-row filtered top-k (pre-filter compaction, search,
+    merge). Prints nothing; timing numbers come from the main run."""
+    import torch
+
+    import cu_roaring_b200 as cr
+
+    torch.cuda.set_device(0)
+    dev = "cuda"
+    U = 1 << 30
+    g = torch.Generator(device=dev).manual_seed(11)
+    ids = c2_upload_ids(torch, g, dev)[:100_000_000]
+    for _ in range(2):
+        cr.upload_from_ids(ids, U).free()
+    del ids
+    torch.cuda.empty_cache()
+    bms, _ = c3_bitmaps(torch, cr, g, U, dev, host=False)
+    for _ in range(2):
+        r = cr.multi_and(bms[:3])
+        cr.enumerate_ids(r, dtype="uint32")
+        r.free()
+    a = cr.upload_from_device_bitset(cr.decompress_to_bitset(bms[0]), U, bitmap_threshold=cr.PROMOTE_ALL)
+    b = cr.upload_from_device_bitset(cr.decompress_to_bitset(bms[1]), U, bitmap_threshold=cr.PROMOTE_ALL)
+    for _ in range(2):
+        cr.set_operation(a, b, cr.AND).free()
+        cr.decompress_to_bitset(a)
+    cand = torch.randint(0, U, (1 << 26,), device=dev, dtype=torch.int64, generator=g).to(torch.int32)
+    for _ in range(2):
+        cr.contains_batch(a, cand)
+    for x in bms + [a, b]:
+        x.free()
+    torch.cuda.empty_cache()
+    n = 1 << 20
+    db = gen_rows(torch, 0, n, dev)
+    tset = choose_tag_set(torch, dev, PASS_TARGET)
+    m = torch.isin(gen_tags(torch, 0, n, dev), tset).any(dim=1)
+    filt = cr.upload_from_ids(torch.nonzero(m).flatten().to(torch.int32), n)
+    q = gen_queries(torch, dev)
+    for _ in range(3):
+        cr.filtered_topk(db, q, K, filter=filt)
+    torch.cuda.synchronize()
+    filt.free()
+
+
 # ------------------------------------------------------------------ main
 
 def main():
@@ -907,7 +957,11 @@ def main():
     ap.add_argument("--secondary", default="all", choices=["all", "topk", "roaring", "none"],
                     help="which secondary measurements run at N=1 (all by default)")
     ap.add_argument("--rows", type=int, default=N_ROWS, help="database rows (profiling runs only)")
+    ap.add_argument("--profile-case", action="store_true", help="run the reduced profiling case (for ncu) and exit")
     args = ap.parse_args()
+    if args.profile_case:
+        profile_case()
+        return
     if args.impl == "reference":
         run_reference(args)
         return
