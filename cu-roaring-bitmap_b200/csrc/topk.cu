@@ -807,9 +807,13 @@ __device__ void make_plan(const uint32_t* count, const PlanArgs a, SearchPlan* p
   *plan = pl;
 }
 
-__global__ void k_plan(const uint32_t* count, const PlanArgs a, SearchPlan* plan)
+__global__ void k_plan(const uint32_t* count, const PlanArgs a, SearchPlan* plan, uint32_t* err0, uint32_t* err1)
 {
-  if (threadIdx.x == 0 && blockIdx.x == 0) make_plan(count, a, plan);
+  if (threadIdx.x == 0 && blockIdx.x == 0) {
+    make_plan(count, a, plan);
+    *err0 = 0u;  // this call's error words start clear
+    *err1 = 0u;
+  }
 }
 
 // One warp per query: spec_used[q] = the j-th largest of the n_vals (<= 256)
@@ -1267,8 +1271,12 @@ __global__ void k_pass_bits(cu_roaring::GpuRoaringView v, uint64_t row_offset, u
 // tile_sums[block] and is added to *count.
 __global__ void __launch_bounds__(256) k_pass_words(DevBitmap b, uint64_t row_offset, uint64_t n_rows,
                                                     uint32_t* out, uint64_t n_words, uint32_t* tile_sums,
-                                                    uint32_t* count)
+                                                    uint32_t* err0, uint32_t* err1)
 {
+  if (blockIdx.x == 0 && threadIdx.x == 0) {  // this call's error words start clear
+    *err0 = 0u;
+    *err1 = 0u;
+  }
   __shared__ uint32_t s_red[32];
   const uint64_t w = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   const uint64_t id0 = row_offset + w * 32;
@@ -1316,10 +1324,7 @@ __global__ void __launch_bounds__(256) k_pass_words(DevBitmap b, uint64_t row_of
   }
   if (w < n_words) out[w] = bits;
   const uint32_t t = block_sum<256>(uint32_t(__popc(w < n_words ? bits : 0u)), s_red);
-  if (threadIdx.x == 0) {
-    tile_sums[blockIdx.x] = t;
-    atomicAdd(count, t);
-  }
+  if (threadIdx.x == 0) tile_sums[blockIdx.x] = t;
 }
 
 // Squared norms, 16 lanes per 128-dim row (16 bytes each).
@@ -1347,16 +1352,17 @@ __global__ void k_row_norms(const uint4* db, uint64_t n_rows, float* out)
 constexpr uint32_t kWordTile = 256;  // pass words per block of the count and compaction kernels
 
 __global__ void __launch_bounds__(kWordTile) k_pass_tile_sums(const uint32_t* pass, uint64_t n_words,
-                                                              uint32_t* tile_sums, uint32_t* total)
+                                                              uint32_t* tile_sums, uint32_t* err0, uint32_t* err1)
 {
+  if (blockIdx.x == 0 && threadIdx.x == 0) {  // this call's error words start clear
+    *err0 = 0u;
+    *err1 = 0u;
+  }
   __shared__ uint32_t s_red[32];
   const uint64_t w = uint64_t(blockIdx.x) * kWordTile + threadIdx.x;
   const uint32_t c = w < n_words ? __popc(pass[w]) : 0u;
   const uint32_t t = block_sum<kWordTile>(c, s_red);
-  if (threadIdx.x == 0) {
-    tile_sums[blockIdx.x] = t;
-    atomicAdd(total, t);
-  }
+  if (threadIdx.x == 0) tile_sums[blockIdx.x] = t;
 }
 
 // idx[] = shard rows whose filter bit is set, ascending; *total = count.
@@ -1371,11 +1377,8 @@ __global__ void __launch_bounds__(kCompactThreads) k_pass_compact(const uint32_t
                                                             uint32_t* idx, uint32_t* total,
                                                             const float* norms, float* comp_norms,
                                                             const uint4* db, uint4* comp, uint32_t cap_rows,
-                                                            const uint32_t* count, const PlanArgs pa,
-                                                            SearchPlan* plan)
+                                                            const PlanArgs pa, SearchPlan* plan)
 {
-  // The pass count is final (the count kernel has finished): plan here.
-  if (blockIdx.x == 0 && threadIdx.x == 0) make_plan(count, pa, plan);
   __shared__ uint32_t s_red[32];
   // Rows of the earlier word tiles: the block's first output slot.
   uint32_t before = 0, all = 0;
@@ -1386,7 +1389,10 @@ __global__ void __launch_bounds__(kCompactThreads) k_pass_compact(const uint32_t
   }
   const uint32_t base = block_sum<kCompactThreads>(before, s_red);
   const uint32_t everything = block_sum<kCompactThreads>(all, s_red);
-  if (blockIdx.x == 0 && threadIdx.x == 0) *total = everything;
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    *total = everything;
+    make_plan(&everything, pa, plan);  // the pass count is final: plan here
+  }
   if (everything > cap_rows) return;  // dense plan: the shard is searched with the bitset
   const uint64_t w = uint64_t(blockIdx.x) * kWordTile + threadIdx.x;
   uint32_t x = (threadIdx.x < kWordTile && w < n_words) ? pass[w] : 0u;
@@ -1604,13 +1610,24 @@ struct Arena {
   }
 };
 
+// The error words of a finished search (and of its exact redo, if any) into
+// the host-visible slot.
+__global__ void k_export_err(const uint32_t* err0, const uint32_t* err1, uint32_t* slot)
+{
+  if (threadIdx.x == 0) {
+    slot[0] = *err0;
+    slot[1] = err1 ? *err1 : 0u;
+  }
+}
+
 // Device-side failures of a search (bounded waits that ran out) are copied to
 // a small ring of page-locked words per host thread and reported by the next
 // call on that thread, or by cr_filtered_topk_check, without making the
 // search itself wait for the device.
 struct ErrorRing {
   static constexpr int kSlots = 8;
-  uint32_t* words = nullptr;  // [kSlots][2]
+  uint32_t* words = nullptr;  // [kSlots][2], mapped page-locked host memory
+  uint32_t* d_words = nullptr;  // the same words' device address
   cudaEvent_t ev[kSlots] = {};
   bool pending[kSlots] = {};
   int next = 0;
@@ -1637,7 +1654,10 @@ struct ErrorRing {
   void record(const uint32_t* d_err0, const uint32_t* d_err1, cudaStream_t s)
   {
     if (!words) {
-      CR_CUDA(cudaMallocHost(reinterpret_cast<void**>(&words), kSlots * 2 * 4));
+      // Mapped page-locked words: one tiny kernel stores a search's error
+      // words straight into them (no copy-engine work on the stream).
+      CR_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&words), kSlots * 2 * 4, cudaHostAllocMapped));
+      CR_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(&d_words), words, 0));
       for (auto& e : ev) CR_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
     }
     const int i = next;
@@ -1649,9 +1669,8 @@ struct ErrorRing {
       if (bad) fail(CR_ERR_DEVICE, "cr_filtered_topk: a pipeline wait timed out on the device (code " +
                                        std::to_string(bad) + ")");
     }
-    CR_CUDA(cudaMemcpyAsync(words + 2 * i, d_err0, 4, cudaMemcpyDeviceToHost, s));
-    if (d_err1) CR_CUDA(cudaMemcpyAsync(words + 2 * i + 1, d_err1, 4, cudaMemcpyDeviceToHost, s));
-    else words[2 * i + 1] = 0;
+    k_export_err<<<1, 32, 0, s>>>(d_err0, d_err1, d_words + 2 * i);
+    CR_CUDA(cudaGetLastError());
     CR_CUDA(cudaEventRecord(ev[i], s));
     pending[i] = true;
   }
@@ -1827,16 +1846,15 @@ void filtered_topk_enqueue(const uint16_t* d_db, const float* d_db_norms, uint64
   tr.n = 0;
   tr.mark("start", s);
 
-  // Control block for the whole call: plan, pass count, both searches' error
-  // words (the fallback reads the first one).
+  // Control block for the whole call: plan and both searches' error words
+  // (the fallback reads the first one). The call's first kernel clears the
+  // error words; the plan is written whole.
   Arena& arena = Arena::get(s);
   arena.reset();
   char* ctl = arena.take<char>(256);
   SearchPlan* plan = reinterpret_cast<SearchPlan*>(ctl);
-  uint32_t* count = reinterpret_cast<uint32_t*>(ctl + 64);
   uint32_t* err0 = reinterpret_cast<uint32_t*>(ctl + 128);
   uint32_t* err1 = reinterpret_cast<uint32_t*>(ctl + 192);
-  CR_CUDA(cudaMemsetAsync(ctl, 0, 256, s));
 
   // Squared norms of the shard rows (L2 only), computed here when not given.
   const float* norms = d_db_norms;
@@ -1868,7 +1886,7 @@ void filtered_topk_enqueue(const uint16_t* d_db, const float* d_db_norms, uint64
   const PlanArgs pa{uint32_t(n_rows), slices, slices * EPI_PARTS, k, spec_capable, uint32_t(cap_rows),
                     spec_override, tiles_override};
   if (!filter) {
-    k_plan<<<1, 32, 0, s>>>(nullptr, pa, plan);
+    k_plan<<<1, 32, 0, s>>>(nullptr, pa, plan, err0, err1);
   } else {
     uint32_t* pass = arena.take<uint32_t>(pass_words * 4 + 16);
     uint32_t* d_total = arena.take<uint32_t>(16);
@@ -1876,14 +1894,14 @@ void filtered_topk_enqueue(const uint16_t* d_db, const float* d_db_norms, uint64
     if (row_offset % 32 == 0) {
       static_assert(kWordTile == 256, "one pass-word block per word tile");
       const DevBitmap b = make_dev(filter, kidx_holder, s);
-      k_pass_words<<<n_wtiles, 256, 0, s>>>(b, row_offset, n_rows, pass, pass_words, tiles, count);
+      k_pass_words<<<n_wtiles, 256, 0, s>>>(b, row_offset, n_rows, pass, pass_words, tiles, err0, err1);
     } else {
       const cu_roaring::GpuRoaringView v =
           cu_roaring::make_view(*reinterpret_cast<const cu_roaring::GpuRoaring*>(filter));
       const uint64_t threads = pass_words * 32;
       const int grid = static_cast<int>(std::min<uint64_t>(div_up(threads, 256), uint64_t(sm_count()) * 16));
       k_pass_bits<<<grid, 256, 0, s>>>(v, row_offset, n_rows, pass, pass_words, filter->universe_size);
-      k_pass_tile_sums<<<n_wtiles, kWordTile, 0, s>>>(pass, pass_words, tiles, count);
+      k_pass_tile_sums<<<n_wtiles, kWordTile, 0, s>>>(pass, pass_words, tiles, err0, err1);
     }
     CR_CUDA(cudaGetLastError());
     tr.mark("pass_bits", s);
@@ -1897,7 +1915,7 @@ void filtered_topk_enqueue(const uint16_t* d_db, const float* d_db_norms, uint64
       k_pass_compact<<<n_wtiles, kCompactThreads, 0, s>>>(pass, pass_words, tiles, n_wtiles, idx, d_total,
                                                     l2 ? norms : nullptr, comp_norms,
                                                     reinterpret_cast<const uint4*>(d_db),
-                                                    reinterpret_cast<uint4*>(comp), uint32_t(cap_rows), count,
+                                                    reinterpret_cast<uint4*>(comp), uint32_t(cap_rows),
                                                     pa, plan);
       CR_CUDA(cudaGetLastError());
     }
