@@ -25,7 +25,8 @@ FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", 
 
 
 def _headers() -> list[Path]:
-    return list(CSRC.glob("*.cuh")) + list((REPO / "include").rglob("*.h*"))
+    inc = REPO / "include"
+    return list(CSRC.glob("*.cuh")) + [p for ext in ("*.h", "*.hpp", "*.cuh") for p in inc.rglob(ext)]
 
 
 def _newest(paths) -> float:

@@ -103,6 +103,102 @@ __global__ void __launch_bounds__(256) k_contains_bitmap(const uint16_t* __restr
   }
 }
 
+// Bulk contains for mixed layouts (ARRAY / BITMAP / RUN, key_index present):
+// kMix candidates per thread move through the lookup in phases (key index;
+// type, offset and cardinality; the first data probe; the ARRAY search), each
+// phase issuing its loads for all kMix candidates before any is consumed, so
+// a thread keeps kMix dependent chains in flight instead of one. ARRAY
+// containers are probed with the view's 64-entry interpolation window; RUN
+// containers (rare in bulk filters) take the view's run search.
+constexpr int kMix = 4;
+__global__ void __launch_bounds__(256) k_contains_mixed(cu_roaring::GpuRoaringView v,
+                                                        const uint32_t* __restrict__ ids, uint64_t n,
+                                                        uint32_t* __restrict__ out)
+{
+  const uint32_t lane = threadIdx.x & 31;
+  const uint64_t n_words = (n + 31) / 32;
+  const uint64_t warp = (uint64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const uint64_t n_warps = (uint64_t(gridDim.x) * blockDim.x) >> 5;
+  const uint8_t* types = reinterpret_cast<const uint8_t*>(v.types);
+  for (uint64_t w0 = warp * kMix; w0 < n_words; w0 += n_warps * kMix) {
+    uint32_t id[kMix], idx[kMix], off[kMix], card[kMix], base[kMix], cnt[kMix];
+    uint8_t ty[kMix];
+    bool hit[kMix];
+#pragma unroll
+    for (int u = 0; u < kMix; ++u) {
+      const uint64_t i = (w0 + u) * 32 + lane;
+      id[u] = i < n ? __ldcs(ids + i) : 0u;
+    }
+#pragma unroll
+    for (int u = 0; u < kMix; ++u) {
+      const uint32_t key = id[u] >> 16;
+      idx[u] = key <= v.max_key ? uint32_t(__ldg(v.key_index + key)) : 0xFFFFu;
+    }
+#pragma unroll
+    for (int u = 0; u < kMix; ++u) {
+      const uint32_t j = idx[u] != 0xFFFFu ? idx[u] : 0u;
+      ty[u] = idx[u] != 0xFFFFu ? __ldg(types + j) : uint8_t(0xFF);
+      off[u] = __ldg(v.offsets + j);
+      card[u] = __ldg(v.cardinalities + j);
+    }
+    // First data probe: the BITMAP word, or the ARRAY window's two ends.
+    uint64_t word[kMix];
+    uint32_t first[kMix], last[kMix];
+#pragma unroll
+    for (int u = 0; u < kMix; ++u) {
+      const uint32_t low = id[u] & 0xFFFFu;
+      word[u] = 0;
+      first[u] = 0;
+      last[u] = 0xFFFFu;
+      base[u] = 0;
+      cnt[u] = card[u];
+      if (ty[u] == uint8_t(cu_roaring::ContainerTypeD::BITMAP)) {
+        word[u] = __ldg(v.bitmap_data + (off[u] >> 3) + (low >> 6));
+      } else if (ty[u] == uint8_t(cu_roaring::ContainerTypeD::ARRAY) && card[u] > 64) {
+        const uint32_t g = (low * card[u]) >> 16;
+        const uint32_t ws = g >= 32 ? min(g - 32, card[u] - 64) : 0u;
+        const uint16_t* a = v.array_data + (off[u] >> 1);
+        first[u] = __ldg(a + ws);
+        last[u] = __ldg(a + ws + 63);
+        base[u] = ws;
+        cnt[u] = 64;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kMix; ++u) {
+      const uint32_t low = id[u] & 0xFFFFu;
+      bool in = false;
+      if (ty[u] == uint8_t(cu_roaring::ContainerTypeD::BITMAP)) {
+        in = (word[u] >> (low & 63u)) & 1ull;
+      } else if (ty[u] == uint8_t(cu_roaring::ContainerTypeD::ARRAY) && card[u] > 0) {
+        uint32_t b = base[u], m = cnt[u];
+        if (card[u] > 64) {  // narrow to the window or to the side of it that must hold `low`
+          if (low < first[u]) { b = 0; m = base[u]; }
+          else if (low > last[u]) { b = base[u] + 64; m = card[u] - b; }
+        }
+        const uint16_t* a = v.array_data + (off[u] >> 1);
+        if (m > 0) {
+          while (m > 1) {
+            const uint32_t h = m >> 1;
+            b = (__ldg(a + b + h - 1) < low) ? b + h : b;
+            m -= h;
+          }
+          in = __ldg(a + b) == low;
+        }
+      } else if (ty[u] == uint8_t(cu_roaring::ContainerTypeD::RUN)) {
+        in = v.run_contains(off[u], uint16_t(card[u]), uint16_t(low));
+      }
+      hit[u] = in != v.negated;
+    }
+#pragma unroll
+    for (int u = 0; u < kMix; ++u) {
+      const uint64_t i = (w0 + u) * 32 + lane;
+      const uint32_t bits = __ballot_sync(0xFFFFFFFFu, hit[u] && i < n);
+      if (lane == 0 && w0 + u < n_words) __stcs(out + w0 + u, bits);
+    }
+  }
+}
+
 // One CTA (256 threads) per output chunk.
 __global__ void __launch_bounds__(256) k_decompress(DevBitmap b, uint32_t* out, uint64_t out_words)
 {
@@ -312,6 +408,10 @@ extern "C" int cr_contains_batch(const cr_gpu_roaring* bm, const uint32_t* d_ids
     const int grid_b = static_cast<int>(std::max<uint64_t>(1, std::min<uint64_t>(want_b, uint64_t(sm_count()) * 8)));
     k_contains_bitmap<<<grid_b, 256, 0, s>>>(v.key_index, v.max_key, v.bitmap_data, v.negated ? 1u : 0u,
                                              d_ids, n, d_out_bits);
+  } else if (mode == 0 && v.key_index != nullptr && v.n_containers > 0) {
+    const uint64_t want_m = (words + 8 * kMix - 1) / (8 * kMix);
+    const int grid_m = static_cast<int>(std::max<uint64_t>(1, std::min<uint64_t>(want_m, uint64_t(sm_count()) * 8)));
+    k_contains_mixed<<<grid_m, 256, 0, s>>>(v, d_ids, n, d_out_bits);
   } else if (mode) {
     k_contains<1><<<grid, 256, 0, s>>>(v, d_ids, n, d_out_bits);
   } else {

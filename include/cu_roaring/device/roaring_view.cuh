@@ -117,7 +117,21 @@ struct GpuRoaringView {
   {
     if (card == 0) return false;
     const uint16_t* a = array_data + (byte_offset >> 1);
-    uint32_t n = card, base = 0;
+    // The sorted lows of a chunk sit near index low * card / 65536 when they
+    // are spread out: look at a 64-entry window around that estimate first
+    // (its two ends in one or two cache lines, so the search inside is cheap)
+    // and narrow the search to the window or to the side of it that must
+    // hold `low`. Exact for any data; only the speed depends on the spread.
+    uint32_t base = 0, n = card;
+    if (card > 64) {
+      const uint32_t g = (static_cast<uint32_t>(low) * card) >> 16;
+      const uint32_t w0 = g >= 32 ? min(g - 32, static_cast<uint32_t>(card) - 64) : 0u;
+      const uint16_t first = __ldg(a + w0), last = __ldg(a + w0 + 63);
+      if (low < first) n = w0;
+      else if (low > last) { base = w0 + 64; n = card - base; }
+      else { base = w0; n = 64; }
+      if (n == 0) return false;
+    }
     while (n > 1) {
       const uint32_t half = n >> 1;
       base = (__ldg(a + base + half - 1) < low) ? base + half : base;
