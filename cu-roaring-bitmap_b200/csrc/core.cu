@@ -232,6 +232,7 @@ DevBitmap make_dev(const cr_gpu_roaring* b, Scratch& holder, cudaStream_t s)
 namespace {
 constexpr int kProfileKinds = 8;
 bool g_profile = false;
+uint32_t g_profile_kinds = 0xFFFFFFFFu;  // which kernel ids cr_profile_enable brackets
 // Every profiled launch since cr_profile_enable(1), as (start, stop) event
 // pairs; the events are kept and reused across enables.
 struct ProfileEvents {
@@ -243,7 +244,7 @@ thread_local ProfileEvents g_prof;
 
 ProfileScope::ProfileScope(int k, cudaStream_t st) : kind(k), s(st), on(g_profile)
 {
-  if (!on || kind < 0 || kind >= kProfileKinds) { on = false; return; }
+  if (!on || kind < 0 || kind >= kProfileKinds || !((g_profile_kinds >> kind) & 1u)) { on = false; return; }
   const size_t i = g_prof.n[kind];
   if (i == g_prof.start[kind].size()) {
     cudaEvent_t a, b;
@@ -265,6 +266,12 @@ ProfileScope::~ProfileScope()
 }  // namespace crb
 
 using namespace crb;
+
+extern "C" int cr_profile_kinds(uint32_t mask)
+{
+  g_profile_kinds = mask;
+  return CR_OK;
+}
 
 extern "C" int cr_profile_enable(int on)
 {

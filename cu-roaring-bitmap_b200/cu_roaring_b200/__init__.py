@@ -36,7 +36,7 @@ EXPORTED_SYMBOLS = (
     "cr_decompress_to_bitset", "cr_decompress_to_bitset_alloc", "cr_enumerate_ids_i64",
     "cr_enumerate_ids_u32", "cr_enumerate_ids_alloc", "cr_enumerate_ids_u32_noalloc", "cr_contains_batch", "cr_filtered_topk",
     "cr_row_norms", "cr_topk_merge", "cr_topk_merge_packed", "cr_upload_portable", "cr_batch_upload_portable", "cr_batch_free",
-    "cr_batch_promote", "cr_batch_multi_and", "cr_batch_decompress", "cr_batch_contains", "cr_filtered_topk_check", "cr_profile_enable", "cr_profile_last_ms", "cr_profile_sum_ms",
+    "cr_batch_promote", "cr_batch_multi_and", "cr_batch_decompress", "cr_batch_contains", "cr_filtered_topk_check", "cr_profile_enable", "cr_profile_kinds", "cr_profile_last_ms", "cr_profile_sum_ms",
     "cr_topk_comm_unique_id", "cr_topk_comm_init", "cr_topk_comm_size", "cr_topk_comm_destroy",
     "cr_filtered_topk_sharded", "cr_upload_portable_ex", "cr_portable_meta", "cr_key_range", "cr_key_slice",
     "cr_concat_key_slices", "cr_test_fail_allocations",
@@ -88,6 +88,7 @@ _sigs = {
     "cr_row_norms": ([_vp, _u64, _u32, _vp, _vp], _i32),
     "cr_topk_merge": ([_vp, _vp, _u32, _u32, _u32, _i32, _vp, _vp, _vp], _i32),
     "cr_profile_enable": ([_i32], _i32),
+    "cr_profile_kinds": ([C.c_uint32], _i32),
     "cr_profile_last_ms": ([_i32, C.POINTER(C.c_float)], _i32),
     "cr_topk_merge_packed": ([C.c_void_p, C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, _i32, C.c_void_p,
                               C.c_void_p, C.c_void_p], _i32),
@@ -600,6 +601,12 @@ def filtered_topk_sharded(comm: TopkComm, db, queries, k: int, metric: int = MET
 
 def profile_enable(on: bool = True) -> None:
     _lib.cr_profile_enable(int(on))
+
+
+def profile_kinds(*kernels: int) -> None:
+    """Bracket only these kernel ids while profiling is on (none given: all)."""
+    mask = 0xFFFFFFFF if not kernels else sum(1 << k for k in set(kernels))
+    _lib.cr_profile_kinds(mask)
 
 
 def profile_mean_ms(kernel: int) -> tuple[float, int]:

@@ -383,6 +383,11 @@ int cr_test_fail_allocations(int64_t after);
 #define CR_KERNEL_TOPK_MERGE 6
 #define CR_KERNEL_TOPK_COMPACT 7 /* pass-row compaction plus the row copy of the pre-filter */
 int cr_profile_enable(int on);
+/* Restricts the bracketing to the kernel ids whose bit is set in `mask`
+ * (default: all). Each bracket is two event records on the launching
+ * stream, which cost device time between short kernels. No reference
+ * counterpart (measurement support). */
+int cr_profile_kinds(uint32_t mask);
 int cr_profile_last_ms(int kernel, float* ms);
 /* Sum of the device times of every profiled launch of `kernel` since
  * profiling was last switched on, and their number (waits for them). */

@@ -141,6 +141,65 @@ def test_upload_rejects_out_of_universe(cr):
         cr.upload_from_ids(np.array([1, 2, 1000], np.uint32), 100)
 
 
+def mixed_chunks(rng, n_chunks, scale=1.0):
+    """Config-2 shapes: sparse (Poisson 2000), dense (Bernoulli 0.3) and run
+    chunks (runs of length [256, 8192]) in thirds, ~5% duplicates, shuffled."""
+    parts = []
+    for c in range(n_chunks):
+        base = c << 16
+        kind = c % 3
+        if kind == 0:
+            m = rng.poisson(2000 * scale)
+            parts.append(base + rng.integers(0, 65536, m, dtype=np.int64))
+        elif kind == 1:
+            parts.append(base + np.flatnonzero(rng.random(65536) < 0.3))
+        else:
+            pos = int(rng.integers(0, 4096))
+            while pos < 65536:
+                ln = int(rng.integers(256, 8193))
+                parts.append(base + np.arange(pos, min(pos + ln, 65536)))
+                pos += ln + int(rng.integers(256, 8193))
+    ids = np.concatenate(parts).astype(np.uint32)
+    ids = np.concatenate([ids, ids[rng.integers(0, ids.size, ids.size // 20)]])
+    rng.shuffle(ids)
+    return ids
+
+
+@pytest.mark.parametrize("case", ["u26", "u26_unaligned", "u31_many_passes", "u26_uniform"])
+def test_upload_large_dense(cr, oracle, l2, torch_, case):
+    """Large dense uploads (>= 2^22 IDs: several scatter passes over chunk
+    slot ranges, more than 32768 chunks, a ragged tail, an unaligned ID
+    pointer) give the oracle's image."""
+    rng = np.random.default_rng(11)
+    if case == "u31_many_passes":
+        u = (1 << 31) + 12345  # 32769 chunks: eight scatter passes
+        ids = rng.integers(0, u, 40_000_037, dtype=np.uint64).astype(np.uint32)
+        thrs = (AUTO,)
+    elif case == "u26_uniform":
+        u = 1 << 26
+        ids = rng.integers(0, u, (1 << 22) + 5, dtype=np.uint64).astype(np.uint32)
+        thrs = (KEEP, ALL)
+    else:
+        u = 1 << 26
+        ids = mixed_chunks(rng, 1024)
+        thrs = (KEEP, ALL, AUTO)
+    assert ids.size >= 1 << 22
+    d = torch_.from_numpy(np.concatenate([np.zeros(1, np.uint32), ids]).view(np.int32)).cuda()
+    src = d[1:] if case == "u26_unaligned" else d[1:].clone()
+    for thr in thrs:
+        ora = oracle.from_ids(ids, u, thr, l2)
+        dev = cr.upload_from_ids(src, u, bitmap_threshold=thr)
+        assert_same_image(dev, ora, f"{case} thr={thr}")
+        dev.free()
+
+
+def test_upload_large_rejects_out_of_universe(cr, torch_):
+    ids = np.arange(0, 1 << 23, dtype=np.uint32)
+    ids[5_000_001] = 1 << 23
+    with pytest.raises(RuntimeError, match="universe"):
+        cr.upload_from_ids(torch_.from_numpy(ids.view(np.int32)).cuda(), 1 << 23)
+
+
 # ------------------------------------------------------------ set algebra
 
 def forced_negated(cr, oracle, words, u):
