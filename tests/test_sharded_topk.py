@@ -16,6 +16,12 @@ import pytest
 
 
 def test_nccl_resolves_and_makes_an_id(built_lib):
+    # The library binds to the NCCL the process has already loaded and only
+    # otherwise opens libnccl.so.2 from the search path. PyTorch ships its own
+    # (newer) copy under the same soname, so a process that uses both loads
+    # torch first, as every user of these bindings does.
+    import torch  # noqa: F401
+
     lib = C.CDLL(str(built_lib))
     buf = C.create_string_buffer(128)
     rc = lib.cr_topk_comm_unique_id(buf, 128)
