@@ -86,6 +86,10 @@ void build_key_index(const uint16_t* keys, uint32_t n, uint16_t* kidx, uint32_t 
                      cudaStream_t s);
 
 int sm_count();
+// Page-locked staging for the small device-to-host readbacks a call waits
+// on (a pageable destination costs a staged copy). Per host thread, grown on
+// demand; the contents are valid until this thread's next call of it.
+void* pinned_stage(size_t bytes);
 // Raises the dynamic shared memory limit of `fn` on the current device.
 // Function attributes are per device, so every device a process launches on
 // gets its own call; later calls on that device are free.

@@ -1,5 +1,6 @@
 // cu_roaring B200 engine — errors, packed allocation, device queries, free,
 // deep copy, threshold resolution.
+#include <algorithm>
 #include <atomic>
 #include <map>
 #include <mutex>
@@ -108,6 +109,25 @@ void alloc_result(cr_gpu_roaring* out, cudaStream_t s)
   out->bitmap_data = out->n_bitmap_containers ? reinterpret_cast<uint64_t*>(base + L.bitmap) : nullptr;
   out->array_data = out->array_pool_bytes ? reinterpret_cast<uint16_t*>(base + L.array) : nullptr;
   out->run_data = out->run_pool_bytes ? reinterpret_cast<uint16_t*>(base + L.run) : nullptr;
+}
+
+void* pinned_stage(size_t bytes)
+{
+  struct Stage {
+    void* p = nullptr;
+    size_t cap = 0;
+    ~Stage() { if (p) cudaFreeHost(p); }
+  };
+  thread_local Stage st;
+  if (bytes > st.cap) {
+    if (st.p) CR_CUDA(cudaFreeHost(st.p));  // every earlier readback has been waited for
+    st.p = nullptr;
+    st.cap = 0;
+    const size_t cap = std::max<size_t>(bytes, 4096);
+    CR_CUDA(cudaHostAlloc(&st.p, cap, cudaHostAllocPortable));
+    st.cap = cap;
+  }
+  return st.p;
 }
 
 int sm_count()

@@ -485,9 +485,10 @@ void kway(const std::vector<const cr_gpu_roaring*>& P, const std::vector<const c
   k_plan_tiles<<<n_tiles, kTile, 0, s>>>(d_ops, tiles);
   k_plan_work<<<n_tiles, kTile, 0, s>>>(d_ops, tiles, n_tiles, work, d_hdr);
   CR_CUDA(cudaGetLastError());
-  WorkTotals h{};
-  CR_CUDA(cudaMemcpyAsync(&h, d_hdr, sizeof(h), cudaMemcpyDeviceToHost, s));
+  WorkTotals* hp = static_cast<WorkTotals*>(pinned_stage(sizeof(WorkTotals)));
+  CR_CUDA(cudaMemcpyAsync(hp, d_hdr, sizeof(WorkTotals), cudaMemcpyDeviceToHost, s));
   CR_CUDA(cudaStreamSynchronize(s));  // sync 1: the work list size
+  const WorkTotals h = *hp;
   if (h.err) fail(CR_ERR_RANGE, "set operation: an operand holds IDs beyond the result universe");
   if (h.n == 0) return;
 
@@ -507,11 +508,12 @@ void kway(const std::vector<const cr_gpu_roaring*>& P, const std::vector<const c
   const uint32_t f_tiles = div_up(h.n, kTile);
   k_final_tiles<<<f_tiles, kTile, 0, s>>>(work, counts, h.n, d_ops, ftiles);
   CR_CUDA(cudaGetLastError());
-  std::vector<FinalTotals> ft(f_tiles);
-  CR_CUDA(cudaMemcpyAsync(ft.data(), ftiles, f_tiles * sizeof(FinalTotals), cudaMemcpyDeviceToHost, s));
+  FinalTotals* ft = static_cast<FinalTotals*>(pinned_stage(f_tiles * sizeof(FinalTotals)));
+  CR_CUDA(cudaMemcpyAsync(ft, ftiles, f_tiles * sizeof(FinalTotals), cudaMemcpyDeviceToHost, s));
   CR_CUDA(cudaStreamSynchronize(s));  // sync 2: the final sizes
   FinalTotals f{};
-  for (auto& x : ft) {
+  for (uint32_t t = 0; t < f_tiles; ++t) {
+    const FinalTotals& x = ft[t];
     f.n += x.n; f.nb += x.nb; f.na += x.na; f.nr += x.nr; f.holes += x.holes; f.ab += x.ab; f.rb += x.rb; f.stored += x.stored;
   }
   out->total_cardinality = negated ? uint64_t(U) - f.stored : f.stored;

@@ -495,9 +495,10 @@ static void build_from_chunks(const ChunkSrc& src, uint32_t max_slots, uint32_t 
   k_plan_emit<<<n_tiles, kPlanTile, 0, s>>>(src, max_slots, stats, d_total, t0, t1, guard, tiles,
                                             n_tiles, plan, d_hdr, d_err);
   CR_CUDA(cudaGetLastError());
-  PlanHeader h{};
-  CR_CUDA(cudaMemcpyAsync(&h, d_hdr, sizeof(h), cudaMemcpyDeviceToHost, s));
+  PlanHeader* hp = static_cast<PlanHeader*>(pinned_stage(sizeof(PlanHeader)));
+  CR_CUDA(cudaMemcpyAsync(hp, d_hdr, sizeof(PlanHeader), cudaMemcpyDeviceToHost, s));
   CR_CUDA(cudaStreamSynchronize(s));
+  const PlanHeader h = *hp;
   if (h.err) fail(CR_ERR_RANGE, "upload: an input ID is >= universe_size");
   out->negated = h.negated != 0;
   out->total_cardinality = h.total_logical;
