@@ -122,34 +122,54 @@ __device__ __forceinline__ uint32_t count_run_starts(const uint64_t w[4], uint64
 }
 
 // One CTA per chunk slot: stats[s] = (c, r, c_complement, r_complement).
+// Two barriers per chunk: one to pass each warp's top bits (set and
+// complement) to the next warp, one for the per-warp sums; the complement's
+// count is the chunk's valid bits minus the set's.
 template <bool VEC>
 __global__ void __launch_bounds__(kEmitThreads) k_analyze(ChunkSrc src, uint32_t max_slots,
                                                           uint4* stats,
                                                           unsigned long long* total)
 {
-  __shared__ uint64_t s_last[kEmitThreads / 32];
-  __shared__ uint32_t s_red[kEmitThreads / 32];
+  __shared__ uint32_t s_last[kEmitThreads / 32];
+  __shared__ uint4 s_red[kEmitThreads / 32];
   const uint32_t s = blockIdx.x;
   if (s >= slot_count(src, max_slots)) return;
   const uint32_t key = src.slot_keys ? src.slot_keys[s] : s;
   const uint32_t valid = chunk_valid_bits(key, src.universe);
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   uint64_t w[4], cw[4];
   load_chunk_words<VEC>(src, s, valid, false, w);
 #pragma unroll
   for (int i = 0; i < 4; ++i) cw[i] = ~w[i] & word_mask(4 * threadIdx.x + i, valid);
-  uint32_t c = 0, cc = 0;
+  uint32_t c = 0;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) { c += __popcll(w[i]); cc += __popcll(cw[i]); }
-  const uint64_t pw = prev_top_bit(w[3], s_last);
-  const uint64_t pc = prev_top_bit(cw[3], s_last);
-  const uint32_t r = count_run_starts(w, pw);
-  const uint32_t cr = count_run_starts(cw, pc);
-  const uint32_t C = block_sum<kEmitThreads>(c, s_red);
-  const uint32_t R = block_sum<kEmitThreads>(r, s_red);
-  const uint32_t CC = block_sum<kEmitThreads>(cc, s_red);
-  const uint32_t CR = block_sum<kEmitThreads>(cr, s_red);
+  for (int i = 0; i < 4; ++i) c += __popcll(w[i]);
+  // Top bits of the previous thread's last words: bit 0 set, bit 1 complement.
+  const uint32_t mine = uint32_t(w[3] >> 63) | (uint32_t(cw[3] >> 63) << 1);
+  uint32_t prev = __shfl_up_sync(0xFFFFFFFFu, mine, 1);
+  if (lane == 31) s_last[warp] = mine;
+  __syncthreads();
+  if (lane == 0) prev = warp ? s_last[warp - 1] : 0u;
+  uint32_t r = count_run_starts(w, prev & 1u);
+  uint32_t cr = count_run_starts(cw, (prev >> 1) & 1u);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    c += __shfl_xor_sync(0xFFFFFFFFu, c, o);
+    r += __shfl_xor_sync(0xFFFFFFFFu, r, o);
+    cr += __shfl_xor_sync(0xFFFFFFFFu, cr, o);
+  }
+  if (lane == 0) s_red[warp] = make_uint4(c, r, cr, 0u);
+  __syncthreads();
   if (threadIdx.x == 0) {
-    stats[s] = make_uint4(C, R, CC, CR);
+    uint32_t C = 0, R = 0, CR = 0;
+#pragma unroll
+    for (int i = 0; i < kEmitThreads / 32; ++i) {
+      const uint4 x = s_red[i];
+      C += x.x;
+      R += x.y;
+      CR += x.z;
+    }
+    stats[s] = make_uint4(C, R, valid - C, CR);
     if (C) atomicAdd(total, static_cast<unsigned long long>(C));
   }
 }

@@ -67,6 +67,7 @@ def lib():
             "or_widen_f16": ([v, u64, v], None),
             "or_row_norms_f32": ([v, u64, u32, v], None),
             "or_cpu_upload_sorted": ([v, u64, u32, u32, v], u64),
+            "or_serialize_portable": ([v, u64, i32, v, u64], u64),
         }
         for name, (a, r) in sig.items():
             f = getattr(_lib, name)
@@ -204,7 +205,6 @@ def serialize_portable(ids, allow_runs: bool = True) -> bytes:
     """Portable Roaring serialization of a set of uint32 IDs (any order, duplicates ok)."""
     a = np.unique(np.asarray(ids, dtype=np.uint32))
     f = lib().or_serialize_portable
-    f.restype = C.c_uint64
     n = f(a.ctypes.data if a.size else None, C.c_uint64(a.size), int(allow_runs), None, C.c_uint64(0))
     buf = (C.c_uint8 * max(1, n))()
     f(a.ctypes.data if a.size else None, C.c_uint64(a.size), int(allow_runs), buf, C.c_uint64(n))
