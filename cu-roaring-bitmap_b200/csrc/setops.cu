@@ -535,7 +535,8 @@ void kway(const std::vector<const cr_gpu_roaring*>& P, const std::vector<const c
   }
   CR_CUDA(cudaMemsetAsync(dst.key_index, 0xFF, (size_t(max_key) + 1) * 2, s));
   k_final_meta<<<f_tiles, kTile, 0, s>>>(work, counts, h.n, ftiles, f_tiles, repack, dst, dst_off);
-  k_final_payload<<<h.n, 256, 0, s>>>(work, counts, dst_off, arr.as<uint16_t>(), blk, dst, repack);
+  if (repack || f.na > 0)  // otherwise every payload already sits where the result wants it
+    k_final_payload<<<h.n, 256, 0, s>>>(work, counts, dst_off, arr.as<uint16_t>(), blk, dst, repack);
   CR_CUDA(cudaGetLastError());
   if (repack) dev_free(blk._alloc_base, s);
   const uint64_t logical = out->total_cardinality;
