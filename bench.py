@@ -1176,8 +1176,9 @@ def main():
                     "d2h_bytes_per_step": N_QUERIES * K * 12},
             # per step and rank: k_pass_words, k_pass_compact, k_topk (prologue),
             # k_spec, k_topk (main), k_merge, k_redo_gate (the guarded exact redo
-            # exits at once unless needed); with N > 1 rank 0's k_merge of the
-            # gathered blocks
+            # exits at once unless needed, after writing the error words to the
+            # host-visible ring); with N > 1 rank 0's k_merge of the gathered
+            # blocks
             "gpu_launches": args.steps * (7 + (1 if world > 1 else 0)),
             "clocks": clocks.summary() if clocks is not None else None,
         }

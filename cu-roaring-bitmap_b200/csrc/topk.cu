@@ -53,6 +53,10 @@
 #include "cu_roaring/device/roaring_warp_query.cuh"
 #include "tcgen05.cuh"
 
+// The error words of a finished search into its host-visible slot (defined
+// with the error ring below; the redo gate tail-launches it).
+__global__ void k_export_err(const uint32_t* err0, const uint32_t* err1, uint32_t* slot);
+
 namespace crb {
 namespace {
 
@@ -1490,14 +1494,23 @@ void merge_launch(const float* ps, const int64_t* pid, uint32_t parts, uint32_t 
 // overflowing candidate array or a speculative bound above some query's k-th
 // best: one block checks the flag, zeroes the redo's counters and tail-launches
 // the search and its merge (they run, in order, once this block has finished).
+// `slot` (host-visible, may be null) receives both passes' error words once
+// the call's work is done: here when no redo runs, else from a tail launch
+// after the redo's search and merge.
 __global__ void __launch_bounds__(1024) k_redo_gate(const uint32_t* guard, uint32_t* zero, uint64_t zero_words,
                                                     uint32_t* err, dim3 grid, const __grid_constant__ CUtensorMap tq,
                                                     const __grid_constant__ CUtensorMap tdb,
                                                     const __grid_constant__ CUtensorMap tcomp, TopkParams tp,
                                                     uint32_t n_lists, const __half* queries, float* out_d,
-                                                    int64_t* out_id)
+                                                    int64_t* out_id, uint32_t* slot)
 {
-  if (!(*reinterpret_cast<const volatile uint32_t*>(guard) & (kErrOverflow | kErrSpec))) return;
+  if (!(*reinterpret_cast<const volatile uint32_t*>(guard) & (kErrOverflow | kErrSpec))) {
+    if (slot && threadIdx.x == 0) {
+      slot[0] = *reinterpret_cast<const volatile uint32_t*>(guard);
+      slot[1] = *reinterpret_cast<const volatile uint32_t*>(err);
+    }
+    return;
+  }
   for (uint64_t i = threadIdx.x; i < zero_words; i += blockDim.x) zero[i] = 0u;
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -1510,6 +1523,7 @@ __global__ void __launch_bounds__(1024) k_redo_gate(const uint32_t* guard, uint3
         tp.part_s, tp.part_id, n_lists, tp.n_queries, tp.k, tp.metric, 0, queries, DIM, out_d, out_id, nullptr, 0,
         nullptr, nullptr, 0, nullptr, 0, 0, nullptr, err, nullptr, nullptr, stride, stride);
     if (cudaGetLastError() != cudaSuccess) atomicOr(err, kErrLaunch);
+    if (slot) ::k_export_err<<<1, 32, 0, cudaStreamTailLaunch>>>(guard, err, slot);
   }
 }
 
@@ -1651,28 +1665,41 @@ struct ErrorRing {
                                 std::to_string(bad) + ")");
     }
   }
-  void record(const uint32_t* d_err0, const uint32_t* d_err1, cudaStream_t s)
+  // The next slot's device address (waiting for its previous search when
+  // more than kSlots are in flight); the caller has its words written on
+  // stream `s`, then calls commit(s).
+  uint32_t* acquire()
   {
     if (!words) {
-      // Mapped page-locked words: one tiny kernel stores a search's error
-      // words straight into them (no copy-engine work on the stream).
       CR_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&words), kSlots * 2 * 4, cudaHostAllocMapped));
       CR_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(&d_words), words, 0));
       for (auto& e : ev) CR_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
     }
     const int i = next;
-    next = (next + 1) % kSlots;
-    if (pending[i]) {  // more than kSlots searches in flight: wait for the oldest
+    if (pending[i]) {
       CR_CUDA(cudaEventSynchronize(ev[i]));
       const uint32_t bad = (words[2 * i] & ~(kErrOverflow | kErrSpec)) | words[2 * i + 1];
       pending[i] = false;
       if (bad) fail(CR_ERR_DEVICE, "cr_filtered_topk: a pipeline wait timed out on the device (code " +
                                        std::to_string(bad) + ")");
     }
-    k_export_err<<<1, 32, 0, s>>>(d_err0, d_err1, d_words + 2 * i);
-    CR_CUDA(cudaGetLastError());
+    return d_words + 2 * i;
+  }
+  void commit(cudaStream_t s)
+  {
+    const int i = next;
+    next = (next + 1) % kSlots;
     CR_CUDA(cudaEventRecord(ev[i], s));
     pending[i] = true;
+  }
+  // A search without a redo gate: one tiny kernel stores its error words
+  // straight into the mapped slot (no copy-engine work on the stream).
+  void record(const uint32_t* d_err0, const uint32_t* d_err1, cudaStream_t s)
+  {
+    uint32_t* slot = acquire();
+    k_export_err<<<1, 32, 0, s>>>(d_err0, d_err1, slot);
+    CR_CUDA(cudaGetLastError());
+    commit(s);
   }
 };
 
@@ -1699,7 +1726,7 @@ struct SearchInput {
 static void run_search(const SearchInput& in, const uint16_t* d_queries, uint32_t n_queries, uint64_t row_offset,
                        uint32_t k, int metric, float* d_out_dist, int64_t* d_out_ids, cudaStream_t s,
                        bool allow_append, bool allow_spec, const uint32_t* guard, uint32_t* err,
-                       bool* used_append)
+                       bool* used_append, uint32_t* err_slot = nullptr)
 {
   set_max_dynamic_smem(reinterpret_cast<const void*>(k_topk<true, false>), int(SMEM_TOTAL));
   set_max_dynamic_smem(reinterpret_cast<const void*>(k_topk<false, false>), int(SMEM_TOTAL));
@@ -1784,7 +1811,7 @@ static void run_search(const SearchInput& in, const uint16_t* d_queries, uint32_
   const dim3 grid(qtiles, slices);
   if (guard) {
     k_redo_gate<<<1, 1024, 0, s>>>(guard, tp.shared_thr, zero_b / 4, err, grid, tq, tdb, tcomp, tp, n_lists,
-                                   reinterpret_cast<const __half*>(d_queries), d_out_dist, d_out_ids);
+                                   reinterpret_cast<const __half*>(d_queries), d_out_dist, d_out_ids, err_slot);
     CR_CUDA(cudaGetLastError());
     Trace::get().mark("redo_gate", s);
     return;
@@ -1942,10 +1969,16 @@ void filtered_topk_enqueue(const uint16_t* d_db, const float* d_db_norms, uint64
   // unless the first search flagged an overflowing candidate array
   // (degenerate score distributions, e.g. massive ties) or a speculative
   // bound above some query's k-th best.
-  if (appended)
+  ErrorRing& ring = ErrorRing::get();
+  if (appended) {
+    // The redo gate also hands the error words to the host-visible ring.
+    uint32_t* slot = ring.acquire();
     run_search(in, d_queries, n_queries, row_offset, k, metric, d_out_dist, d_out_ids, s, false, false, err0, err1,
-               &unused);
-  ErrorRing::get().record(err0, appended ? err1 : nullptr, s);
+               &unused, slot);
+    ring.commit(s);
+  } else {
+    ring.record(err0, nullptr, s);
+  }
   tr.mark("search", s);
   tr.print();
 }
