@@ -1275,12 +1275,18 @@ __global__ void k_pass_bits(cu_roaring::GpuRoaringView v, uint64_t row_offset, u
 // tile_sums[block] and is added to *count.
 __global__ void __launch_bounds__(256) k_pass_words(DevBitmap b, uint64_t row_offset, uint64_t n_rows,
                                                     uint32_t* out, uint64_t n_words, uint32_t* tile_sums,
-                                                    uint32_t* err0, uint32_t* err1)
+                                                    uint32_t* err0, uint32_t* err1, uint4* zero,
+                                                    uint64_t zero_vec)
 {
   if (blockIdx.x == 0 && threadIdx.x == 0) {  // this call's error words start clear
     *err0 = 0u;
     *err1 = 0u;
   }
+  // The search's counters and published bounds start at zero (null: the
+  // caller clears them).
+  for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; zero && i < zero_vec;
+       i += uint64_t(gridDim.x) * blockDim.x)
+    zero[i] = make_uint4(0u, 0u, 0u, 0u);
   __shared__ uint32_t s_red[32];
   const uint64_t w = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   const uint64_t id0 = row_offset + w * 32;
@@ -1718,6 +1724,21 @@ struct SearchInput {
   const float* chunk_min;  // L2: least norm per 32 searched rows
 };
 
+// Bytes of the block a search needs cleared before it runs: per-query shared
+// thresholds, published bounds, candidate counts, published best three
+// (the same sizing as run_search's).
+static size_t search_zero_bytes(uint32_t n_queries, uint32_t k, uint32_t slices, bool allow_append, bool allow_spec)
+{
+  const uint32_t n_lists = slices * EPI_PARTS;
+  const uint32_t jth = (k + n_lists - 1) / n_lists;
+  const bool append = allow_append && jth <= 3 && n_lists <= kMaxListsMerge;
+  const bool spec_capable = append && allow_spec && 3 * n_lists <= 256;
+  const size_t pub_b = size_t(n_queries) * n_lists * 4;
+  const size_t cnt_b = append ? size_t(n_queries) * n_lists * 4 : 0;
+  const size_t top_b = spec_capable ? size_t(n_queries) * n_lists * 3 * 4 : 0;
+  return size_t(n_queries) * 4 + pub_b + cnt_b + top_b;
+}
+
 // One search over the planned rows plus the per-query merge, stream-ordered.
 // Append mode (candidate arrays, speculative bound) unless disabled; `guard`
 // makes every kernel of it a no-op unless that error word asks for a redo;
@@ -1726,7 +1747,7 @@ struct SearchInput {
 static void run_search(const SearchInput& in, const uint16_t* d_queries, uint32_t n_queries, uint64_t row_offset,
                        uint32_t k, int metric, float* d_out_dist, int64_t* d_out_ids, cudaStream_t s,
                        bool allow_append, bool allow_spec, const uint32_t* guard, uint32_t* err,
-                       bool* used_append, uint32_t* err_slot = nullptr)
+                       bool* used_append, uint32_t* err_slot = nullptr, char* cleared = nullptr)
 {
   set_max_dynamic_smem(reinterpret_cast<const void*>(k_topk<true, false>), int(SMEM_TOTAL));
   set_max_dynamic_smem(reinterpret_cast<const void*>(k_topk<false, false>), int(SMEM_TOTAL));
@@ -1760,15 +1781,19 @@ static void run_search(const SearchInput& in, const uint16_t* d_queries, uint32_
   // by one memset: per-query shared thresholds, published bounds, candidate
   // counts, published best three.
   const size_t zero_b = size_t(n_queries) * 4 + pub_b + cnt_b + top_b;
-  char* p = Arena::get(s).take<char>(zero_b + 256 + list_b * 2 + cbuf_b * 2 + part_b * 12 + cand_b * 2 + spec_b + 256);
+  // `cleared`: the block, already zeroed by the call's first kernel.
+  char* p = Arena::get(s).take<char>((cleared ? 0 : zero_b) + 256 + list_b * 2 + cbuf_b * 2 + part_b * 12 +
+                                     cand_b * 2 + spec_b + 256);
+  char* const rest = p + (cleared ? 0 : zero_b);
+  if (cleared) p = cleared;
   TopkParams tp{};
   tp.err = err;
   tp.shared_thr = reinterpret_cast<uint32_t*>(p); p += size_t(n_queries) * 4;
   tp.pub = reinterpret_cast<uint32_t*>(p); p += pub_b;
   if (append) { tp.cand_cnt = reinterpret_cast<uint32_t*>(p); p += cnt_b; }
   if (spec_capable) { tp.pub_top = reinterpret_cast<uint32_t*>(p); p += top_b; }
-  if (!guard) CR_CUDA(cudaMemsetAsync(tp.shared_thr, 0, zero_b, s));
-  p = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(p) + 255) & ~uintptr_t(255));
+  if (!guard && !cleared) CR_CUDA(cudaMemsetAsync(tp.shared_thr, 0, zero_b, s));
+  p = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(rest) + 255) & ~uintptr_t(255));
   tp.n_queries = n_queries;
   tp.k = k;
   tp.metric = metric;
@@ -1909,6 +1934,12 @@ void filtered_topk_enqueue(const uint16_t* d_db, const float* d_db_norms, uint64
   // Up to 3/4 of the rows passing, copying the passing rows (512 B of HBM
   // traffic each) is cheaper than searching every row with the mask.
   const uint64_t cap_rows = filter ? std::max<uint64_t>(1, n_rows * 3 / 4) : 0;
+  // The first search's zeroed block: cleared by k_pass_words when that
+  // kernel runs with enough threads (at most 8 16-byte stores each), else
+  // by a memset inside the search.
+  const size_t zero_bytes = (search_zero_bytes(n_queries, k, slices, true, true) + 15) & ~size_t(15);
+  const bool clear_in_pass = filter && row_offset % 32 == 0 && uint64_t(n_wtiles) * 256 * 8 >= zero_bytes / 16;
+  char* cleared = clear_in_pass ? arena.take<char>(zero_bytes) : nullptr;
   Scratch kidx_holder;
   const PlanArgs pa{uint32_t(n_rows), slices, slices * EPI_PARTS, k, spec_capable, uint32_t(cap_rows),
                     spec_override, tiles_override};
@@ -1921,7 +1952,8 @@ void filtered_topk_enqueue(const uint16_t* d_db, const float* d_db_norms, uint64
     if (row_offset % 32 == 0) {
       static_assert(kWordTile == 256, "one pass-word block per word tile");
       const DevBitmap b = make_dev(filter, kidx_holder, s);
-      k_pass_words<<<n_wtiles, 256, 0, s>>>(b, row_offset, n_rows, pass, pass_words, tiles, err0, err1);
+      k_pass_words<<<n_wtiles, 256, 0, s>>>(b, row_offset, n_rows, pass, pass_words, tiles, err0, err1,
+                                            reinterpret_cast<uint4*>(cleared), zero_bytes / 16);
     } else {
       const cu_roaring::GpuRoaringView v =
           cu_roaring::make_view(*reinterpret_cast<const cu_roaring::GpuRoaring*>(filter));
@@ -1963,7 +1995,7 @@ void filtered_topk_enqueue(const uint16_t* d_db, const float* d_db_norms, uint64
   CR_CUDA(cudaGetLastError());
   bool appended = false, unused = false;
   run_search(in, d_queries, n_queries, row_offset, k, metric, d_out_dist, d_out_ids, s, true, true, nullptr, err0,
-             &appended);
+             &appended, nullptr, cleared);
   // The exact redo with per-list merging, which needs neither candidate
   // capacity nor a speculative bound: every kernel of it returns at once
   // unless the first search flagged an overflowing candidate array
